@@ -1,0 +1,198 @@
+/*
+ * kvoff.h - C ABI of the B200 KV-cache offload copy path (libkvoff.so).
+ *
+ * Every entry point takes plain pointers, 64-bit sizes and an opaque CUDA
+ * stream handle (a cudaStream_t cast to void*; NULL is the legacy default
+ * stream). Nothing here synchronizes the host: all GPU work is enqueued on
+ * the given stream. Every function returns a kvoff_status; on failure
+ * kvoff_last_error() describes the problem for the calling thread.
+ *
+ * Paged pool geometry. The engine's KV pool is a tensor
+ *     pool[2, L, NB, BS, H, D]     (K/V, layer, block, token, KV head, dim)
+ * (nanovllm/engine/model_runner.py:120). One KV block is 2*L "chunks"; each
+ * chunk holds BS*H rows of D contiguous elements and sits at
+ *     pool + c * chunk_stride + block_id * block_stride      (c in [0, 2L))
+ * counted in elements (bf16 here), so chunk_stride = NB*BS*H*D and
+ * block_stride = BS*H*D for a contiguous pool. A "row" is one (token, KV
+ * head) vector of D elements. A saved block ("slot") is laid out densely as
+ * [2, L, BS, H, D] (cpu_prefix_cache.py:94), so row r of chunk c lands at
+ * slot + (c * rows_per_chunk + r) * D.
+ *
+ * FP8 slots store the payload [2, L, BS, H, D] float8_e4m3fn and one bf16
+ * scale per row, [2, L, BS, H, 1] (cpu_prefix_cache.py:96-100, 204-206).
+ */
+#ifndef KVOFF_H_
+#define KVOFF_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define KVOFF_API __attribute__((visibility("default")))
+#else
+#define KVOFF_API
+#endif
+
+#define KVOFF_ABI_VERSION 1
+
+/* Status codes returned by every entry point. */
+enum kvoff_status {
+  KVOFF_OK = 0,
+  KVOFF_EINVAL = 1,    /* bad argument: null pointer, size, alignment, block id */
+  KVOFF_ECUDA = 2,     /* a CUDA runtime call failed */
+  KVOFF_EINJECTED = 3, /* failure injected by kvoff_debug_fail_next */
+  KVOFF_ENOMEM = 4,    /* host allocation / pinning failed */
+  KVOFF_EDEVICE = 5    /* a kernel reported a device-side error flag */
+};
+
+/* Directions and methods for kvoff_copy_blocks. */
+enum kvoff_direction { KVOFF_SAVE = 0, KVOFF_RESTORE = 1 };
+enum kvoff_copy_method {
+  KVOFF_COPY_ENGINE = 0, /* cudaMemcpy2DAsync over the 2L strided chunks (DMA engine) */
+  KVOFF_COPY_TMA = 1,    /* cp.async.bulk gather/scatter kernel; slots must be device memory */
+  KVOFF_COPY_SM = 2      /* 16-byte vector copy kernel; slots may be mapped pinned host memory */
+};
+
+/* ABI version of the loaded library (KVOFF_ABI_VERSION at build time). */
+KVOFF_API int32_t kvoff_abi_version(void);
+
+/* Message of the last failure on this thread ("" when none). */
+KVOFF_API const char* kvoff_last_error(void);
+
+/*
+ * Host-side fault injection for tests: the next `count` calls of entry point
+ * `op` (its name without the "kvoff_" prefix, e.g. "fp8_save_blocks") fail
+ * with KVOFF_EINJECTED before enqueuing any work. count = 0 clears it.
+ * Replaces the reference tests' monkeypatching of torch.Tensor.copy_
+ * (bench/test_cpu_prefix_cache.py:113-123, 133-143), which cannot reach
+ * native copies.
+ */
+KVOFF_API int kvoff_debug_fail_next(const char* op, int32_t count);
+
+/*
+ * Device-side error flags of bounded waits in this library's kernels on
+ * `device` (0 = none). clear != 0 resets them. Synchronizes `device`.
+ */
+KVOFF_API int kvoff_device_error(int32_t device, int32_t* flags, int32_t clear);
+
+/*
+ * FP8 save: gather `count` KV blocks of a bf16 paged pool and quantize each
+ * row to float8_e4m3fn with one bf16 scale per row:
+ *     scale   = bf16_rne(max(f32(amax|x|) / 448, 1e-30))
+ *     payload = e4m3_rne(clamp(f32(x) / f32(scale), -448, 448))
+ * Replaces fp8_quantize (nanovllm/engine/cpu_prefix_cache.py:20-24) as used
+ * by CPUBlockCache._quantize (:225-234) on the pool view cache[:, :, block_id]
+ * (:305). payload_dst[i] / scale_dst[i] receive block_ids[i]'s slot; they
+ * must be device-accessible: device memory (staging) or the device alias of
+ * mapped pinned host memory (zero-copy save). max_ctas <= 0 picks a full grid.
+ */
+KVOFF_API int kvoff_fp8_save_blocks(const void* pool, int64_t num_chunks, int64_t chunk_stride,
+                                    int64_t block_stride, int64_t num_blocks,
+                                    int64_t rows_per_chunk, int64_t head_dim,
+                                    const int64_t* block_ids, int64_t count,
+                                    void* const* payload_dst, void* const* scale_dst,
+                                    int32_t max_ctas, void* stream);
+
+/*
+ * FP8 restore: dequantize slots into pool blocks,
+ *     x = bf16_rne(f32(payload) * f32(scale))
+ * Replaces fp8_dequantize (cpu_prefix_cache.py:27-28) as used by
+ * CPUBlockCache._dequantize (:236-243) into cache[:, :, block_id] (:373).
+ * Sources must be device-accessible (staging or mapped pinned host).
+ */
+KVOFF_API int kvoff_fp8_restore_blocks(void* pool, int64_t num_chunks, int64_t chunk_stride,
+                                       int64_t block_stride, int64_t num_blocks,
+                                       int64_t rows_per_chunk, int64_t head_dim,
+                                       const int64_t* block_ids, int64_t count,
+                                       const void* const* payload_src,
+                                       const void* const* scale_src, int32_t max_ctas,
+                                       void* stream);
+
+/*
+ * Staged FP8 save: quantize up to `staging_blocks` blocks at a time into the
+ * contiguous device staging buffers, then drain each block with two
+ * cudaMemcpyAsync calls into host_payload[i] / host_scale[i] (pinned host).
+ * Replaces CPUBlockCache._quantize's device-staging branch
+ * (cpu_prefix_cache.py:227-234, staging from _stage :217-223).
+ */
+KVOFF_API int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks,
+                                           int64_t chunk_stride, int64_t block_stride,
+                                           int64_t num_blocks, int64_t rows_per_chunk,
+                                           int64_t head_dim, const int64_t* block_ids,
+                                           int64_t count, void* const* host_payload,
+                                           void* const* host_scale, void* staging_payload,
+                                           void* staging_scale, int64_t staging_blocks,
+                                           void* stream);
+
+/*
+ * Staged FP8 restore: copy each slot host->device into staging (two
+ * cudaMemcpyAsync per block), then dequantize into the pool. Replaces
+ * CPUBlockCache._dequantize's CUDA branch (cpu_prefix_cache.py:237-243).
+ */
+KVOFF_API int kvoff_fp8_restore_blocks_staged(void* pool, int64_t num_chunks,
+                                              int64_t chunk_stride, int64_t block_stride,
+                                              int64_t num_blocks, int64_t rows_per_chunk,
+                                              int64_t head_dim, const int64_t* block_ids,
+                                              int64_t count, const void* const* host_payload,
+                                              const void* const* host_scale,
+                                              void* staging_payload, void* staging_scale,
+                                              int64_t staging_blocks, void* stream);
+
+/*
+ * Byte-exact block passthrough (BF16 mode): move whole blocks between the
+ * pool and dense slots. Strides and sizes are in BYTES here. direction
+ * KVOFF_SAVE copies pool -> slots[i], KVOFF_RESTORE slots[i] -> pool.
+ * Replaces payload.copy_(source) (cpu_prefix_cache.py:319) and
+ * target.copy_(entry.kv) (:386). Method KVOFF_COPY_TMA needs device slots
+ * and 16-byte alignment of every address and of chunk_bytes.
+ */
+KVOFF_API int kvoff_copy_blocks(void* pool, int64_t num_chunks, int64_t chunk_stride_bytes,
+                                int64_t block_stride_bytes, int64_t num_blocks,
+                                int64_t chunk_bytes, const int64_t* block_ids, int64_t count,
+                                void* const* slots, int32_t direction, int32_t method,
+                                int32_t max_ctas, void* stream);
+
+/*
+ * Slot-mapping scatter of fresh K/V rows into the paged cache:
+ *     for i < num_tokens with slot = slot_mapping[i] != -1:
+ *         k_cache[slot * row_bytes ...] = key[i * key_stride_bytes ...] (row_bytes)
+ *         v_cache[slot * row_bytes ...] = value[i * value_stride_bytes ...]
+ * Replaces store_kvcache / store_kvcache_kernel
+ * (nanovllm/layers/attention.py:10-40). Negative slots are skipped; slots
+ * >= num_slots are skipped and counted into *bad_slots when it is non-null
+ * (device memory). No allocation and no host synchronization, so it can be
+ * captured in a CUDA graph.
+ */
+KVOFF_API int kvoff_store_kvcache(const void* key, int64_t key_stride_bytes, const void* value,
+                                  int64_t value_stride_bytes, void* k_cache, void* v_cache,
+                                  int64_t row_bytes, const int32_t* slot_mapping,
+                                  int64_t num_tokens, int64_t num_slots, int32_t* bad_slots,
+                                  void* stream);
+
+/*
+ * Pinned host slab: mmap `bytes`, prefer NUMA node `numa_node` (-1: no
+ * preference), page-lock it with cudaHostRegister(Portable | Mapped) and
+ * return the host pointer and its device alias for zero-copy kernels.
+ * Replaces the pin_memory=True slab chunks of CPUBlockCache._grow
+ * (cpu_prefix_cache.py:199-208).
+ */
+KVOFF_API int kvoff_host_alloc(uint64_t bytes, int32_t numa_node, void** host_ptr,
+                               void** device_ptr);
+
+/* Unregister and unmap a slab from kvoff_host_alloc. */
+KVOFF_API int kvoff_host_free(void* host_ptr);
+
+/* NUMA node closest to CUDA device `device` (-1 when unknown). */
+KVOFF_API int kvoff_device_numa_node(int32_t device, int32_t* numa_node);
+
+/* cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream). */
+KVOFF_API int kvoff_memcpy(void* dst, const void* src, uint64_t bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVOFF_H_ */

@@ -1,0 +1,491 @@
+// FP8 save (gather + per-row quantize) and restore (dequantize + scatter) of
+// paged KV blocks, plus the staged variants that drain through device
+// staging buffers with cudaMemcpyAsync.
+//
+// Work decomposition: a "unit" is a tile of up to kTile consecutive rows of
+// one chunk (one K/V x layer slice) of one block. Rows of a tile are
+// contiguous in both the pool and the slot, so every warp instruction moves
+// contiguous bytes. A persistent grid strides over units.
+//
+// Save, fast path (D = 8 * LANES, LANES in {4, 8, 16, 32}): LANES lanes own
+// one row, each loading 16 bytes (8 bf16) with a non-coherent streaming load.
+// The row amax is an integer max over |bf16| bit patterns (exact, and NaN
+// wins because NaN patterns sort above Inf), reduced with xor-shuffles inside
+// the lane group. Each lane then writes 8 payload bytes; the tile's scales are
+// collected in shared memory and written as one contiguous run, which keeps
+// zero-copy (PCIe) scale writes coalesced.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "codec.cuh"
+#include "runtime.h"
+
+namespace kvoff {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTile = 256;       // rows per unit
+constexpr int kMaxBatch = 128;   // blocks per launch (kernel-parameter table)
+constexpr int kUnroll = 4;       // independent 16-byte loads in flight per lane
+
+struct Geometry {
+  int64_t num_chunks;      // 2 * layers
+  int64_t chunk_stride;    // elements between (kv, layer) chunks in the pool
+  int64_t block_stride;    // elements between blocks in the pool
+  int64_t rows_per_chunk;  // block_size * kv_heads
+  int64_t tiles_per_chunk;
+  int32_t head_dim;
+};
+
+struct BlockTable {
+  int64_t block[kMaxBatch];
+  void* payload[kMaxBatch];  // slot payload (save: destination, restore: source)
+  void* scale[kMaxBatch];
+};
+
+struct Unit {
+  int64_t slot_row;   // row index inside the slot, c * rows_per_chunk + row0
+  int64_t pool_elem;  // element offset of the tile's first row in the pool
+  int idx;            // position in the block table
+  int rows;           // rows in this tile
+};
+
+__device__ __forceinline__ Unit decode_unit(int64_t u, const Geometry& g,
+                                            const BlockTable& t) {
+  const int64_t per_block = g.num_chunks * g.tiles_per_chunk;
+  Unit r;
+  r.idx = (int)(u / per_block);
+  const int64_t rem = u - (int64_t)r.idx * per_block;
+  const int64_t c = rem / g.tiles_per_chunk;
+  const int64_t row0 = (rem - c * g.tiles_per_chunk) * kTile;
+  const int64_t left = g.rows_per_chunk - row0;
+  r.rows = (int)(left < kTile ? left : kTile);
+  r.slot_row = c * g.rows_per_chunk + row0;
+  r.pool_elem = c * g.chunk_stride + t.block[r.idx] * g.block_stride + row0 * g.head_dim;
+  return r;
+}
+
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint2 ld_stream8(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p));
+  return v;
+}
+
+// Quantize 8 bf16 (four packed words) of a row with scale bits `sb`.
+__device__ __forceinline__ uint2 quantize8(const uint32_t w[4], uint32_t sb) {
+  uint32_t b[4];
+  if (sb < 0x7F80u) {
+    const float s = bf16_to_f32(sb);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = quant_input(bf16_to_f32(w[j] & 0xFFFFu), s);
+      const float hi = quant_input(bf16_to_f32(w[j] >> 16), s);
+      b[j] = f32x2_to_e4m3x2(lo, hi);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      b[j] = special_row_byte(w[j] & 0xFFFFu, sb) | (special_row_byte(w[j] >> 16, sb) << 8);
+  }
+  return make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
+}
+
+template <int LANES>
+__global__ void __launch_bounds__(kThreads)
+    fp8_save_kernel(const uint16_t* __restrict__ pool, const Geometry g,
+                    const __grid_constant__ BlockTable t, int64_t units) {
+  constexpr int kRowsPerWarp = 32 / LANES;
+  constexpr int kRowsPerIter = kRowsPerWarp * kWarps;
+  __shared__ uint16_t s_scale[kTile];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane / LANES;
+  const int li = lane % LANES;
+  const int D = 8 * LANES;
+
+  for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+    const Unit un = decode_unit(u, g, t);
+    const uint16_t* src = pool + un.pool_elem;
+    uint8_t* dst = static_cast<uint8_t*>(t.payload[un.idx]) + un.slot_row * D;
+    for (int base = 0; base < un.rows; base += kRowsPerIter * kUnroll) {
+      uint4 v[kUnroll];
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int r = base + k * kRowsPerIter + warp * kRowsPerWarp + sub;
+        v[k] = r < un.rows ? ld_stream16(src + (int64_t)r * D + li * 8) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int r = base + k * kRowsPerIter + warp * kRowsPerWarp + sub;
+        const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+        const uint32_t m = __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                                    __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
+        uint32_t amax = max(m & 0xFFFFu, m >> 16);
+#pragma unroll
+        for (int off = LANES / 2; off > 0; off >>= 1)
+          amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+        const uint32_t sb = scale_from_amax(amax);
+        if (r < un.rows) {
+          *reinterpret_cast<uint2*>(dst + (int64_t)r * D + li * 8) = quantize8(w, sb);
+          if (li == 0) s_scale[r] = (uint16_t)sb;
+        }
+      }
+    }
+    __syncthreads();
+    uint16_t* sdst = static_cast<uint16_t*>(t.scale[un.idx]) + un.slot_row;
+    for (int j = threadIdx.x; j < un.rows; j += kThreads) sdst[j] = s_scale[j];
+    __syncthreads();
+  }
+}
+
+template <int LANES>
+__global__ void __launch_bounds__(kThreads)
+    fp8_restore_kernel(uint16_t* __restrict__ pool, const Geometry g,
+                       const __grid_constant__ BlockTable t, int64_t units) {
+  constexpr int kRowsPerWarp = 32 / LANES;
+  constexpr int kRowsPerIter = kRowsPerWarp * kWarps;
+  __shared__ uint16_t s_scale[kTile];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane / LANES;
+  const int li = lane % LANES;
+  const int D = 8 * LANES;
+
+  for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+    const Unit un = decode_unit(u, g, t);
+    const uint8_t* psrc = static_cast<const uint8_t*>(t.payload[un.idx]) + un.slot_row * D;
+    const uint16_t* ssrc = static_cast<const uint16_t*>(t.scale[un.idx]) + un.slot_row;
+    uint16_t* dst = pool + un.pool_elem;
+    for (int j = threadIdx.x; j < un.rows; j += kThreads) s_scale[j] = ssrc[j];
+    __syncthreads();
+    for (int base = 0; base < un.rows; base += kRowsPerIter * kUnroll) {
+      uint2 v[kUnroll];
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int r = base + k * kRowsPerIter + warp * kRowsPerWarp + sub;
+        v[k] = r < un.rows ? ld_stream8(psrc + (int64_t)r * D + li * 8) : make_uint2(0, 0);
+      }
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int r = base + k * kRowsPerIter + warp * kRowsPerWarp + sub;
+        if (r >= un.rows) continue;
+        const float s = bf16_to_f32(s_scale[r]);
+        const uint32_t pairs[4] = {v[k].x & 0xFFFFu, v[k].x >> 16, v[k].y & 0xFFFFu, v[k].y >> 16};
+        uint32_t out[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = e4m3x2_to_f32x2(pairs[j]);
+          out[j] = f32_to_bf16_rne(__fmul_rn(f.x, s)) | (f32_to_bf16_rne(__fmul_rn(f.y, s)) << 16);
+        }
+        *reinterpret_cast<uint4*>(dst + (int64_t)r * D + li * 8) =
+            make_uint4(out[0], out[1], out[2], out[3]);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Any head_dim and alignment: one thread per row, two passes over the row.
+__global__ void fp8_save_generic_kernel(const uint16_t* __restrict__ pool, const Geometry g,
+                                        const __grid_constant__ BlockTable t, int count) {
+  const int64_t D = g.head_dim;
+  const int64_t rows_per_block = g.num_chunks * g.rows_per_chunk;
+  const int64_t total = rows_per_block * count;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < total;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int idx = (int)(q / rows_per_block);
+    const int64_t slot_row = q - idx * rows_per_block;
+    const int64_t c = slot_row / g.rows_per_chunk;
+    const int64_t r = slot_row - c * g.rows_per_chunk;
+    const uint16_t* src = pool + c * g.chunk_stride + t.block[idx] * g.block_stride + r * D;
+    uint32_t amax = 0;
+    for (int64_t j = 0; j < D; ++j) amax = max(amax, (uint32_t)(src[j] & 0x7FFFu));
+    const uint32_t sb = scale_from_amax(amax);
+    uint8_t* dst = static_cast<uint8_t*>(t.payload[idx]) + slot_row * D;
+    for (int64_t j = 0; j < D; ++j) {
+      const uint32_t x = src[j];
+      dst[j] = (uint8_t)(sb < 0x7F80u
+                             ? f32x2_to_e4m3x2(quant_input(bf16_to_f32(x), bf16_to_f32(sb)), 0.f) & 0xFFu
+                             : special_row_byte(x, sb));
+    }
+    static_cast<uint16_t*>(t.scale[idx])[slot_row] = (uint16_t)sb;
+  }
+}
+
+__global__ void fp8_restore_generic_kernel(uint16_t* __restrict__ pool, const Geometry g,
+                                           const __grid_constant__ BlockTable t, int count) {
+  const int64_t D = g.head_dim;
+  const int64_t rows_per_block = g.num_chunks * g.rows_per_chunk;
+  const int64_t total = rows_per_block * count;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < total;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int idx = (int)(q / rows_per_block);
+    const int64_t slot_row = q - idx * rows_per_block;
+    const int64_t c = slot_row / g.rows_per_chunk;
+    const int64_t r = slot_row - c * g.rows_per_chunk;
+    uint16_t* dst = pool + c * g.chunk_stride + t.block[idx] * g.block_stride + r * D;
+    const uint8_t* src = static_cast<const uint8_t*>(t.payload[idx]) + slot_row * D;
+    const float s = bf16_to_f32(static_cast<const uint16_t*>(t.scale[idx])[slot_row]);
+    for (int64_t j = 0; j < D; ++j)
+      dst[j] = (uint16_t)f32_to_bf16_rne(__fmul_rn(e4m3x2_to_f32x2(src[j]).x, s));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+
+struct Args {
+  const char* op;
+  void* pool;
+  Geometry g;
+  int64_t num_blocks;
+  const int64_t* block_ids;
+  int64_t count;
+};
+
+int validate(Args& a, int64_t num_chunks, int64_t chunk_stride, int64_t block_stride,
+             int64_t rows_per_chunk, int64_t head_dim) {
+  if (a.count < 0) return fail(KVOFF_EINVAL, "kvoff_%s: negative count", a.op);
+  if (a.count > 0 && (a.pool == nullptr || a.block_ids == nullptr))
+    return fail(KVOFF_EINVAL, "kvoff_%s: null pool or block_ids", a.op);
+  if (num_chunks <= 0 || rows_per_chunk <= 0 || head_dim <= 0 || head_dim > (1 << 20) ||
+      chunk_stride < 0 || block_stride < 0 || a.num_blocks <= 0)
+    return fail(KVOFF_EINVAL, "kvoff_%s: bad geometry", a.op);
+  for (int64_t i = 0; i < a.count; ++i)
+    if (a.block_ids[i] < 0 || a.block_ids[i] >= a.num_blocks)
+      return fail(KVOFF_EINVAL, "kvoff_%s: block id %lld out of range [0, %lld)", a.op,
+                  (long long)a.block_ids[i], (long long)a.num_blocks);
+  a.g.num_chunks = num_chunks;
+  a.g.chunk_stride = chunk_stride;
+  a.g.block_stride = block_stride;
+  a.g.rows_per_chunk = rows_per_chunk;
+  a.g.tiles_per_chunk = (rows_per_chunk + kTile - 1) / kTile;
+  a.g.head_dim = (int32_t)head_dim;
+  return KVOFF_OK;
+}
+
+bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+// Lanes per row for the vectorized kernels, or 0 for the generic path.
+int vector_lanes(const Args& a, void* const* payload, void* const* scale) {
+  int lanes = 0;
+  switch (a.g.head_dim) {
+    case 32: lanes = 4; break;
+    case 64: lanes = 8; break;
+    case 128: lanes = 16; break;
+    case 256: lanes = 32; break;
+    default: return 0;
+  }
+  if (!aligned(a.pool, 16) || (a.g.chunk_stride % 8) != 0 || (a.g.block_stride % 8) != 0)
+    return 0;
+  for (int64_t i = 0; i < a.count; ++i)
+    if (!aligned(payload[i], 8) || !aligned(scale[i], 2)) return 0;
+  return lanes;
+}
+
+template <bool kSave>
+const void* pick_kernel(int lanes) {
+  if (kSave) {
+    switch (lanes) {
+      case 4: return (const void*)fp8_save_kernel<4>;
+      case 8: return (const void*)fp8_save_kernel<8>;
+      case 16: return (const void*)fp8_save_kernel<16>;
+      case 32: return (const void*)fp8_save_kernel<32>;
+      default: return (const void*)fp8_save_generic_kernel;
+    }
+  }
+  switch (lanes) {
+    case 4: return (const void*)fp8_restore_kernel<4>;
+    case 8: return (const void*)fp8_restore_kernel<8>;
+    case 16: return (const void*)fp8_restore_kernel<16>;
+    case 32: return (const void*)fp8_restore_kernel<32>;
+    default: return (const void*)fp8_restore_generic_kernel;
+  }
+}
+
+// Launch one kernel per group of <= kMaxBatch blocks.
+template <bool kSave>
+int launch(const Args& a, void* const* payload, void* const* scale, int32_t max_ctas,
+           cudaStream_t stream) {
+  for (int64_t i = 0; i < a.count; ++i)
+    if (payload[i] == nullptr || scale[i] == nullptr)
+      return fail(KVOFF_EINVAL, "kvoff_%s: null slot pointer at %lld", a.op, (long long)i);
+  const int lanes = vector_lanes(a, payload, scale);
+  const void* kernel = pick_kernel<kSave>(lanes);
+  for (int64_t first = 0; first < a.count; first += kMaxBatch) {
+    const int n = (int)((a.count - first) < kMaxBatch ? (a.count - first) : kMaxBatch);
+    BlockTable t;
+    for (int i = 0; i < n; ++i) {
+      t.block[i] = a.block_ids[first + i];
+      t.payload[i] = payload[first + i];
+      t.scale[i] = scale[first + i];
+    }
+    if (lanes != 0) {
+      const int64_t units = (int64_t)n * a.g.num_chunks * a.g.tiles_per_chunk;
+      const int64_t grid = grid_for(units, kernel, kThreads, 0, max_ctas);
+      if (kSave) {
+        switch (lanes) {
+          case 4: fp8_save_kernel<4><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
+          case 8: fp8_save_kernel<8><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
+          case 16: fp8_save_kernel<16><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
+          default: fp8_save_kernel<32><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
+        }
+      } else {
+        switch (lanes) {
+          case 4: fp8_restore_kernel<4><<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, units); break;
+          case 8: fp8_restore_kernel<8><<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, units); break;
+          case 16: fp8_restore_kernel<16><<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, units); break;
+          default: fp8_restore_kernel<32><<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, units); break;
+        }
+      }
+    } else {
+      const int64_t rows = (int64_t)n * a.g.num_chunks * a.g.rows_per_chunk;
+      const int64_t grid = grid_for((rows + kThreads - 1) / kThreads, kernel, kThreads, 0, max_ctas);
+      if (kSave)
+        fp8_save_generic_kernel<<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, n);
+      else
+        fp8_restore_generic_kernel<<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, n);
+    }
+    KVOFF_TRY(cuda_status(cudaGetLastError(), kSave ? "fp8 save launch" : "fp8 restore launch"));
+  }
+  return KVOFF_OK;
+}
+
+int64_t payload_bytes(const Geometry& g) { return g.num_chunks * g.rows_per_chunk * g.head_dim; }
+int64_t scale_bytes(const Geometry& g) { return g.num_chunks * g.rows_per_chunk * 2; }
+
+}  // namespace
+}  // namespace kvoff
+
+using namespace kvoff;
+
+extern "C" {
+
+int kvoff_fp8_save_blocks(const void* pool, int64_t num_chunks, int64_t chunk_stride,
+                          int64_t block_stride, int64_t num_blocks, int64_t rows_per_chunk,
+                          int64_t head_dim, const int64_t* block_ids, int64_t count,
+                          void* const* payload_dst, void* const* scale_dst, int32_t max_ctas,
+                          void* stream) {
+  if (injected("fp8_save_blocks")) return KVOFF_EINJECTED;
+  Args a{"fp8_save_blocks", const_cast<void*>(pool), {}, num_blocks, block_ids, count};
+  KVOFF_TRY(validate(a, num_chunks, chunk_stride, block_stride, rows_per_chunk, head_dim));
+  if (count == 0) return ok();
+  if (payload_dst == nullptr || scale_dst == nullptr)
+    return fail(KVOFF_EINVAL, "kvoff_fp8_save_blocks: null destination table");
+  KVOFF_TRY(launch<true>(a, payload_dst, scale_dst, max_ctas, static_cast<cudaStream_t>(stream)));
+  return ok();
+}
+
+int kvoff_fp8_restore_blocks(void* pool, int64_t num_chunks, int64_t chunk_stride,
+                             int64_t block_stride, int64_t num_blocks, int64_t rows_per_chunk,
+                             int64_t head_dim, const int64_t* block_ids, int64_t count,
+                             const void* const* payload_src, const void* const* scale_src,
+                             int32_t max_ctas, void* stream) {
+  if (injected("fp8_restore_blocks")) return KVOFF_EINJECTED;
+  Args a{"fp8_restore_blocks", pool, {}, num_blocks, block_ids, count};
+  KVOFF_TRY(validate(a, num_chunks, chunk_stride, block_stride, rows_per_chunk, head_dim));
+  if (count == 0) return ok();
+  if (payload_src == nullptr || scale_src == nullptr)
+    return fail(KVOFF_EINVAL, "kvoff_fp8_restore_blocks: null source table");
+  KVOFF_TRY(launch<false>(a, const_cast<void* const*>(payload_src),
+                          const_cast<void* const*>(scale_src), max_ctas,
+                          static_cast<cudaStream_t>(stream)));
+  return ok();
+}
+
+int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks, int64_t chunk_stride,
+                                 int64_t block_stride, int64_t num_blocks,
+                                 int64_t rows_per_chunk, int64_t head_dim,
+                                 const int64_t* block_ids, int64_t count,
+                                 void* const* host_payload, void* const* host_scale,
+                                 void* staging_payload, void* staging_scale,
+                                 int64_t staging_blocks, void* stream) {
+  if (injected("fp8_save_blocks_staged")) return KVOFF_EINJECTED;
+  Args a{"fp8_save_blocks_staged", const_cast<void*>(pool), {}, num_blocks, block_ids, count};
+  KVOFF_TRY(validate(a, num_chunks, chunk_stride, block_stride, rows_per_chunk, head_dim));
+  if (count == 0) return ok();
+  if (host_payload == nullptr || host_scale == nullptr || staging_payload == nullptr ||
+      staging_scale == nullptr || staging_blocks <= 0)
+    return fail(KVOFF_EINVAL, "kvoff_fp8_save_blocks_staged: null buffer or no staging");
+  for (int64_t i = 0; i < count; ++i)
+    if (host_payload[i] == nullptr || host_scale[i] == nullptr)
+      return fail(KVOFF_EINVAL, "kvoff_fp8_save_blocks_staged: null host slot at %lld",
+                  (long long)i);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t pb = payload_bytes(a.g), sb = scale_bytes(a.g);
+  const int64_t group = staging_blocks < kMaxBatch ? staging_blocks : kMaxBatch;
+  void* pdst[kMaxBatch];
+  void* sdst[kMaxBatch];
+  for (int64_t first = 0; first < count; first += group) {
+    const int64_t n = (count - first) < group ? (count - first) : group;
+    for (int64_t i = 0; i < n; ++i) {
+      pdst[i] = static_cast<uint8_t*>(staging_payload) + i * pb;
+      sdst[i] = static_cast<uint8_t*>(staging_scale) + i * sb;
+    }
+    Args sub = a;
+    sub.block_ids = block_ids + first;
+    sub.count = n;
+    KVOFF_TRY(launch<true>(sub, pdst, sdst, 0, s));
+    for (int64_t i = 0; i < n; ++i) {
+      KVOFF_TRY(cuda_status(cudaMemcpyAsync(host_payload[first + i], pdst[i], pb,
+                                            cudaMemcpyDefault, s), "staged save payload copy"));
+      KVOFF_TRY(cuda_status(cudaMemcpyAsync(host_scale[first + i], sdst[i], sb,
+                                            cudaMemcpyDefault, s), "staged save scale copy"));
+    }
+  }
+  return ok();
+}
+
+int kvoff_fp8_restore_blocks_staged(void* pool, int64_t num_chunks, int64_t chunk_stride,
+                                    int64_t block_stride, int64_t num_blocks,
+                                    int64_t rows_per_chunk, int64_t head_dim,
+                                    const int64_t* block_ids, int64_t count,
+                                    const void* const* host_payload,
+                                    const void* const* host_scale, void* staging_payload,
+                                    void* staging_scale, int64_t staging_blocks, void* stream) {
+  if (injected("fp8_restore_blocks_staged")) return KVOFF_EINJECTED;
+  Args a{"fp8_restore_blocks_staged", pool, {}, num_blocks, block_ids, count};
+  KVOFF_TRY(validate(a, num_chunks, chunk_stride, block_stride, rows_per_chunk, head_dim));
+  if (count == 0) return ok();
+  if (host_payload == nullptr || host_scale == nullptr || staging_payload == nullptr ||
+      staging_scale == nullptr || staging_blocks <= 0)
+    return fail(KVOFF_EINVAL, "kvoff_fp8_restore_blocks_staged: null buffer or no staging");
+  for (int64_t i = 0; i < count; ++i)
+    if (host_payload[i] == nullptr || host_scale[i] == nullptr)
+      return fail(KVOFF_EINVAL, "kvoff_fp8_restore_blocks_staged: null host slot at %lld",
+                  (long long)i);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t pb = payload_bytes(a.g), sb = scale_bytes(a.g);
+  const int64_t group = staging_blocks < kMaxBatch ? staging_blocks : kMaxBatch;
+  void* psrc[kMaxBatch];
+  void* ssrc[kMaxBatch];
+  for (int64_t first = 0; first < count; first += group) {
+    const int64_t n = (count - first) < group ? (count - first) : group;
+    for (int64_t i = 0; i < n; ++i) {
+      psrc[i] = static_cast<uint8_t*>(staging_payload) + i * pb;
+      ssrc[i] = static_cast<uint8_t*>(staging_scale) + i * sb;
+      KVOFF_TRY(cuda_status(cudaMemcpyAsync(psrc[i], host_payload[first + i], pb,
+                                            cudaMemcpyDefault, s), "staged restore payload copy"));
+      KVOFF_TRY(cuda_status(cudaMemcpyAsync(ssrc[i], host_scale[first + i], sb,
+                                            cudaMemcpyDefault, s), "staged restore scale copy"));
+    }
+    Args sub = a;
+    sub.block_ids = block_ids + first;
+    sub.count = n;
+    KVOFF_TRY(launch<false>(sub, psrc, ssrc, 0, s));
+  }
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,103 @@
+// Slot-mapping scatter of fresh K/V rows into the paged cache (the prefill /
+// decode store that runs once per layer per step).
+//
+// Token i's K row (row_bytes, at key + i * key_stride_bytes) goes to
+// k_cache + slot * row_bytes, and likewise for V; slot = slot_mapping[i],
+// and -1 marks a padded token that is skipped. The copy is a pure byte move,
+// so any cache dtype is moved bit-exactly. A CTA of 128 threads owns one token
+// at a time: the slot index is loaded once per CTA iteration into a register
+// broadcast, and the K and V rows move with the widest unit (16, 8, 4, 2 or 1
+// bytes) that every address and stride allows. Offsets are 64-bit.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "runtime.h"
+
+namespace kvoff {
+namespace {
+
+constexpr int kThreads = 128;
+
+template <typename V>
+__global__ void __launch_bounds__(kThreads)
+    store_kvcache_kernel(const uint8_t* __restrict__ key, int64_t key_stride,
+                         const uint8_t* __restrict__ value, int64_t value_stride,
+                         uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
+                         int64_t row_bytes, const int32_t* __restrict__ slot_mapping,
+                         int64_t num_tokens, int64_t num_slots, int32_t* bad_slots) {
+  const int64_t vecs = row_bytes / (int64_t)sizeof(V);
+  for (int64_t i = blockIdx.x; i < num_tokens; i += gridDim.x) {
+    const int64_t slot = __ldg(slot_mapping + i);
+    if (slot < 0) continue;
+    if (slot >= num_slots) {
+      if (threadIdx.x == 0 && bad_slots != nullptr) atomicAdd(bad_slots, 1);
+      continue;
+    }
+    const V* ks = reinterpret_cast<const V*>(key + i * key_stride);
+    const V* vs = reinterpret_cast<const V*>(value + i * value_stride);
+    V* kd = reinterpret_cast<V*>(k_cache + slot * row_bytes);
+    V* vd = reinterpret_cast<V*>(v_cache + slot * row_bytes);
+    for (int64_t j = threadIdx.x; j < vecs; j += kThreads) {
+      const V k = __ldg(ks + j);
+      const V v = __ldg(vs + j);
+      kd[j] = k;
+      vd[j] = v;
+    }
+  }
+}
+
+template <typename V>
+int launch(const void* key, int64_t ks, const void* value, int64_t vs, void* kc, void* vc,
+           int64_t row_bytes, const int32_t* slots, int64_t n, int64_t num_slots, int32_t* bad,
+           cudaStream_t stream) {
+  const void* kernel = (const void*)store_kvcache_kernel<V>;
+  const int64_t grid = grid_for(n, kernel, kThreads, 0, 0);
+  store_kvcache_kernel<V><<<grid, kThreads, 0, stream>>>(
+      static_cast<const uint8_t*>(key), ks, static_cast<const uint8_t*>(value), vs,
+      static_cast<uint8_t*>(kc), static_cast<uint8_t*>(vc), row_bytes, slots, n, num_slots, bad);
+  return cuda_status(cudaGetLastError(), "store_kvcache launch");
+}
+
+}  // namespace
+}  // namespace kvoff
+
+using namespace kvoff;
+
+extern "C" int kvoff_store_kvcache(const void* key, int64_t key_stride_bytes, const void* value,
+                                   int64_t value_stride_bytes, void* k_cache, void* v_cache,
+                                   int64_t row_bytes, const int32_t* slot_mapping,
+                                   int64_t num_tokens, int64_t num_slots, int32_t* bad_slots,
+                                   void* stream) {
+  if (injected("store_kvcache")) return KVOFF_EINJECTED;
+  if (num_tokens < 0 || row_bytes <= 0 || num_slots < 0 || key_stride_bytes < 0 ||
+      value_stride_bytes < 0)
+    return fail(KVOFF_EINVAL, "kvoff_store_kvcache: bad sizes");
+  if (num_tokens == 0) return ok();
+  if (key == nullptr || value == nullptr || k_cache == nullptr || v_cache == nullptr ||
+      slot_mapping == nullptr)
+    return fail(KVOFF_EINVAL, "kvoff_store_kvcache: null pointer");
+  // Widest unit dividing every base address, row stride and the row length.
+  uintptr_t bits = reinterpret_cast<uintptr_t>(key) | reinterpret_cast<uintptr_t>(value) |
+                   reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+                   (uintptr_t)key_stride_bytes | (uintptr_t)value_stride_bytes |
+                   (uintptr_t)row_bytes;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc;
+  if ((bits & 15u) == 0)
+    rc = launch<uint4>(key, key_stride_bytes, value, value_stride_bytes, k_cache, v_cache,
+                       row_bytes, slot_mapping, num_tokens, num_slots, bad_slots, s);
+  else if ((bits & 7u) == 0)
+    rc = launch<uint2>(key, key_stride_bytes, value, value_stride_bytes, k_cache, v_cache,
+                       row_bytes, slot_mapping, num_tokens, num_slots, bad_slots, s);
+  else if ((bits & 3u) == 0)
+    rc = launch<uint32_t>(key, key_stride_bytes, value, value_stride_bytes, k_cache, v_cache,
+                          row_bytes, slot_mapping, num_tokens, num_slots, bad_slots, s);
+  else if ((bits & 1u) == 0)
+    rc = launch<uint16_t>(key, key_stride_bytes, value, value_stride_bytes, k_cache, v_cache,
+                          row_bytes, slot_mapping, num_tokens, num_slots, bad_slots, s);
+  else
+    rc = launch<uint8_t>(key, key_stride_bytes, value, value_stride_bytes, k_cache, v_cache,
+                         row_bytes, slot_mapping, num_tokens, num_slots, bad_slots, s);
+  if (rc != KVOFF_OK) return rc;
+  return ok();
+}

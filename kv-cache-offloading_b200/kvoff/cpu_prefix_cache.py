@@ -1,0 +1,590 @@
+"""Drop-in CPU block tier for the nano-vllm engine, with B200-native copies.
+
+This module replaces nanovllm/engine/cpu_prefix_cache.py of the reference
+(xxdydx/KV-Cache-Offloading). Its surface is unchanged: CPUBlockCache with the
+same constructor, properties, public methods, the hooks the block manager calls
+(_preserve_before_recycle, _preserve_on_release, before_block_reuse,
+before_block_use, _entry_for, _copy_entry, _prefetched_blocks) and the private
+attributes the reference tests read (_copy_stream, _restore_stream, _slabs,
+_scale_slabs, _slot_view, _entries, _SLAB_CHUNK_BYTES). Bookkeeping - keys,
+budget, slot recycling, publish-after-copy, error behaviour and messages -
+follows the reference (cpu_prefix_cache.py:44-448).
+
+What changes is the copy path for a CUDA pool. Instead of about ten ATen
+launches plus torch copies per block, a save is one libkvoff call on the copy
+stream: a fused gather + FP8 quantize kernel feeding a DMA drain into a
+NUMA-local pinned slab slot (or writing the slot directly over PCIe), or one
+strided DMA for BF16. Restores mirror it on the restore stream. Stream and
+event ordering is the reference's: a save starts after the current stream's
+writes of the block and after earlier restores that read the slot; a restore
+starts after its own save; block reuse waits for pending copies. A pool on the
+CPU (the reference's host-only test mode) keeps the reference's synchronous
+torch copies and quantizer below.
+"""
+
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from math import prod
+
+import torch
+
+# Pinned memory is allocated in chunks of about this size: one allocation and
+# one page-locking call cover many slots.
+_SLAB_CHUNK_BYTES = 1 << 30
+
+
+# Largest finite float8_e4m3fn magnitude.
+_FP8_MAX = 448.0
+
+
+def fp8_quantize(source: torch.Tensor, payload: torch.Tensor, scale: torch.Tensor):
+    """float8_e4m3fn payload plus one scale (in scale's dtype) per last-dim vector.
+
+    The scale is rounded to its storage dtype first and the payload divides by
+    the rounded value, so dequantization is its exact inverse up to e4m3 rounding.
+    """
+    amax = source.abs().amax(dim=-1, keepdim=True).to(torch.float32)
+    scale.copy_(torch.clamp_min(amax / _FP8_MAX, 1e-30))
+    ratio = source.to(torch.float32) / scale.to(torch.float32)
+    payload.copy_(ratio.clamp_(-_FP8_MAX, _FP8_MAX))
+
+
+def fp8_dequantize(payload: torch.Tensor, scale: torch.Tensor, target: torch.Tensor):
+    """target = payload * scale, computed in target's dtype."""
+    torch.mul(payload.to(target.dtype), scale, out=target)
+
+
+@dataclass(frozen=True)
+class _CPUBlock:
+    token_ids: tuple[int, ...]
+    kv: torch.Tensor  # slot view [K/V, layer, token, KV head, head dim]
+    slot: int
+    scale: torch.Tensor | None = None  # FP8: [K/V, layer, token, KV head, 1]
+    saved: torch.cuda.Event | None = None  # CUDA: the save into `slot` has finished
+
+
+class CPUCacheFullError(MemoryError):
+    """The configured payload budget cannot admit another block."""
+
+
+# Copy methods for CUDA pools. FP8: "staged" (kernel into device staging,
+# DMA drain) or "mapped" (kernel reads/writes the pinned slot over PCIe).
+# BF16: "engine" (one strided DMA per block), "tma" (cp.async.bulk gather into
+# device staging + DMA) or "sm" (vector-copy kernel over PCIe). Override with
+# KVOFF_FP8_SAVE / KVOFF_FP8_RESTORE / KVOFF_BF16_SAVE / KVOFF_BF16_RESTORE.
+DEFAULT_MODES = {"fp8_save": "staged", "fp8_restore": "staged",
+                 "bf16_save": "engine", "bf16_restore": "engine"}
+_MODE_CHOICES = {"fp8_save": ("staged", "mapped"), "fp8_restore": ("staged", "mapped"),
+                 "bf16_save": ("engine", "tma", "sm"), "bf16_restore": ("engine", "tma", "sm")}
+
+
+def _transfer_modes() -> dict[str, str]:
+    modes = {}
+    for key, default in DEFAULT_MODES.items():
+        value = os.environ.get(f"KVOFF_{key.upper()}", default)
+        if value not in _MODE_CHOICES[key]:
+            raise ValueError(f"KVOFF_{key.upper()} must be one of {_MODE_CHOICES[key]}")
+        modes[key] = value
+    return modes
+
+
+class CPUBlockCache:
+    """Bounded pinned-host store of full KV blocks keyed by chained prefix hash.
+
+    Call from the engine-owning thread between steps. The byte budget counts
+    payloads (FP8: e4m3 payload plus one bf16 scale per token and KV head).
+    Restored GPU blocks are ordinary recyclable blocks; the CPU copy lives until
+    discard / clear / close. On CUDA all copies are asynchronous on the copy
+    stream (and a separate restore stream with split_streams=True, so both PCIe
+    directions run at once); call synchronize() before reading slots on the
+    host. automatic / save_on_release / prefetch / hybrid integrate with the
+    block manager exactly as in the reference engine.
+    """
+
+    def __init__(self, runner, block_manager, max_bytes: int, *,
+                 automatic: bool = False, save_on_release: bool = False, preallocate: bool = False,
+                 prefetch: bool = False, split_streams: bool = False, fp8: bool = False,
+                 hybrid: tuple[float, float, float] | None = None):
+        if type(max_bytes) is not int or max_bytes <= 0:
+            raise ValueError("max_bytes must be a positive integer")
+        if runner.world_size != 1:
+            raise NotImplementedError("CPU prefix blocks currently require TP=1")
+        if not automatic and (save_on_release or prefetch or hybrid):
+            raise ValueError("save_on_release, prefetch and hybrid require automatic=True")
+        if hybrid is not None and (len(hybrid) != 3 or min(hybrid) < 0):
+            raise ValueError("hybrid needs three nonnegative cost coefficients")
+        pool = runner.kv_cache
+        layout_ok = (pool.ndim == 6 and pool.shape[0] == 2 and min(pool.shape) > 0
+                     and pool.shape[2] == len(block_manager.blocks)
+                     and pool.shape[3] == block_manager.block_size
+                     and runner.block_size == block_manager.block_size)
+        if not layout_ok:
+            raise ValueError("KV pool layout does not match the block manager")
+        if pool.device.type not in ("cpu", "cuda"):
+            raise ValueError("KV pool must be on CPU or CUDA")
+        self._cache = pool
+        self._manager = block_manager
+        self._fp8 = fp8
+        self._shape = (2, pool.shape[1], *pool.shape[3:])
+        self._scale_shape = (*self._shape[:-1], 1)
+        self._dtype = torch.float8_e4m3fn if fp8 else pool.dtype
+        self._payload_bytes = prod(self._shape) * self._dtype.itemsize
+        self._scale_bytes = prod(self._scale_shape) * pool.element_size() if fp8 else 0
+        self._block_bytes = self._payload_bytes + self._scale_bytes
+        self._max_bytes = max_bytes
+        self._capacity = max_bytes // self._block_bytes
+        self._entries: dict[int, _CPUBlock] = {}
+        self._slabs: list[torch.Tensor] = []
+        self._scale_slabs: list[torch.Tensor] = []
+        self._slab_owners: list = []  # PinnedSlab per chunk (CUDA pools)
+        self._free_slots: list[int] = []
+        self._num_slots = 0
+        self._hybrid = hybrid
+        self._save_on_release = save_on_release
+        self._prefetch = prefetch
+        self._prefetched_blocks = 0
+        self._saved_blocks = 0
+        self._restored_blocks = 0
+        self._budget_skips = 0
+        self._on_cuda = pool.device.type == "cuda"
+        self._copy_stream = self._restore_stream = None
+        self._slot_reads: dict[int, torch.cuda.Event] = {}  # slot -> last restore reading it
+        self._pending_saves: dict[int, torch.cuda.Event] = {}  # GPU block -> save done
+        self._pending_restores: dict[int, torch.cuda.Event] = {}  # GPU block -> restore done
+        self._staging: dict = {}
+        if self._on_cuda:
+            from kvoff import ops  # the native library is required for CUDA pools
+
+            self._ops = ops
+            self._geometry = ops.geometry(pool)
+            if fp8 and pool.dtype != torch.bfloat16:
+                raise ValueError("fp8=True needs a bf16 KV pool")
+            self._modes = _transfer_modes()
+            self._copy_stream = torch.cuda.Stream(pool.device)
+            self._restore_stream = (torch.cuda.Stream(pool.device) if split_streams
+                                    else self._copy_stream)
+        if automatic:
+            if block_manager._cpu_prefix_cache is not None:
+                raise RuntimeError("block manager already has an automatic CPU cache")
+            block_manager._cpu_prefix_cache = self
+        if preallocate:
+            while self._num_slots < self._capacity:
+                self._grow()
+
+    # -- properties ---------------------------------------------------------
+
+    @property
+    def max_bytes(self) -> int:
+        return self._max_bytes
+
+    @property
+    def block_bytes(self) -> int:
+        return self._block_bytes
+
+    @property
+    def bytes_used(self) -> int:
+        return len(self._entries) * self._block_bytes
+
+    @property
+    def reserved_bytes(self) -> int:
+        return self._num_slots * self._block_bytes
+
+    @property
+    def closed(self) -> bool:
+        return self._cache is None
+
+    @property
+    def automatic(self) -> bool:
+        return not self.closed and self._manager._cpu_prefix_cache is self
+
+    @property
+    def prefetch_enabled(self) -> bool:
+        return self._prefetch
+
+    @property
+    def hybrid(self) -> tuple[float, float, float] | None:
+        return self._hybrid
+
+    @hybrid.setter
+    def hybrid(self, costs: tuple[float, float, float] | None):
+        """Split-admission costs, e.g. after measure_restore_s_per_block()."""
+        if costs is not None:
+            if not self.automatic:
+                raise ValueError("hybrid requires an automatic cache")
+            if len(costs) != 3 or min(costs) < 0:
+                raise ValueError("hybrid needs three nonnegative cost coefficients")
+            costs = tuple(float(c) for c in costs)
+        self._hybrid = costs
+
+    @property
+    def fp8(self) -> bool:
+        return self._fp8
+
+    @property
+    def prefetched_blocks(self) -> int:
+        return self._prefetched_blocks
+
+    @property
+    def stats(self) -> dict[str, int]:
+        return {"saved_blocks": self._saved_blocks, "restored_blocks": self._restored_blocks,
+                "budget_skips": self._budget_skips}
+
+    def __len__(self):
+        return len(self._entries)
+
+    def __contains__(self, prefix_hash: int):
+        return prefix_hash in self._entries
+
+    def _require_open(self):
+        if self.closed:
+            raise RuntimeError("CPU prefix cache is closed")
+
+    # -- slots ----------------------------------------------------------------
+
+    def _grow(self):
+        """Add one slab chunk of slots (pinned and NUMA-local for CUDA pools)."""
+        count = min(max(1, _SLAB_CHUNK_BYTES // self._block_bytes),
+                    self._capacity - self._num_slots)
+        if self._on_cuda:
+            from kvoff.slab import PinnedSlab
+
+            scale_offset = -(-count * self._payload_bytes // 256) * 256
+            slab = PinnedSlab(scale_offset + count * self._scale_bytes,
+                              device=self._cache.device.index)
+            payload = slab.view(0, (count, *self._shape), self._dtype)
+            scales = (slab.view(scale_offset, (count, *self._scale_shape), self._cache.dtype)
+                      if self._fp8 else None)
+            self._slab_owners.append(slab)
+        else:
+            payload = torch.empty((count, *self._shape), dtype=self._dtype, device="cpu")
+            scales = (torch.empty((count, *self._scale_shape), dtype=self._cache.dtype,
+                                  device="cpu") if self._fp8 else None)
+        self._slabs.append(payload)
+        if self._fp8:
+            self._scale_slabs.append(scales)
+        first = self._num_slots
+        self._free_slots.extend(range(first + count - 1, first - 1, -1))
+        self._num_slots += count
+
+    def _locate(self, slot: int) -> tuple[int, int]:
+        for chunk, slab in enumerate(self._slabs):
+            if slot < len(slab):
+                return chunk, slot
+            slot -= len(slab)
+        raise IndexError(slot)
+
+    def _slot_view(self, slot: int) -> tuple[torch.Tensor, torch.Tensor | None]:
+        chunk, index = self._locate(slot)
+        return self._slabs[chunk][index], self._scale_slabs[chunk][index] if self._fp8 else None
+
+    def _stage(self, stream) -> tuple[torch.Tensor, torch.Tensor | None]:
+        """Per-stream device staging (FP8 payload + scales, or one raw block).
+
+        Work on one stream runs in order, so reusing its staging is safe.
+        """
+        if stream not in self._staging:
+            device = self._cache.device
+            if self._fp8:
+                self._staging[stream] = (
+                    torch.empty(self._payload_bytes, dtype=torch.uint8, device=device),
+                    torch.empty(self._scale_bytes, dtype=torch.uint8, device=device))
+            else:
+                self._staging[stream] = (
+                    torch.empty(self._payload_bytes, dtype=torch.uint8, device=device), None)
+        return self._staging[stream]
+
+    # -- device copies (CUDA pools) ---------------------------------------------
+
+    def _slot_pointers(self, slot: int, mapped: bool) -> tuple[int, int]:
+        chunk, index = self._locate(slot)
+        payload = self._slabs[chunk][index]
+        scale = self._scale_slabs[chunk][index] if self._fp8 else None
+        if not mapped:
+            return payload.data_ptr(), scale.data_ptr() if scale is not None else 0
+        owner = self._slab_owners[chunk]
+        return (owner.device_alias(payload),
+                owner.device_alias(scale) if scale is not None else 0)
+
+    def _device_save(self, pool: torch.Tensor, block_id: int, slot: int, stream):
+        """Enqueue pool block -> slot on `stream` (the current stream inside)."""
+        ops, modes = self._ops, self._modes
+        if self._fp8:
+            mapped = modes["fp8_save"] == "mapped"
+            payload, scale = self._slot_pointers(slot, mapped)
+            if mapped:
+                ops.save_fp8(pool, [block_id], [payload], [scale], stream=stream)
+            else:
+                staged, staged_scale = self._stage(stream)
+                ops.save_fp8_staged(pool, [block_id], [payload], [scale], staged, staged_scale,
+                                    stream=stream)
+            return
+        method = modes["bf16_save"]
+        payload, _ = self._slot_pointers(slot, method == "sm")
+        if method == "tma":
+            staged, _ = self._stage(stream)
+            ops.copy_blocks(pool, [block_id], [staged.data_ptr()], method=ops.COPY_TMA,
+                            stream=stream)
+            ops.memcpy(payload, staged.data_ptr(), self._payload_bytes, device=pool.device,
+                       stream=stream)
+        else:
+            ops.copy_blocks(pool, [block_id], [payload], stream=stream,
+                            method=ops.COPY_SM if method == "sm" else ops.COPY_ENGINE)
+
+    def _device_restore(self, pool: torch.Tensor, block_id: int, payload: int, scale: int,
+                        mapped_payload: int, mapped_scale: int, stream):
+        """Enqueue slot -> pool block on `stream`."""
+        ops, modes = self._ops, self._modes
+        if self._fp8:
+            if modes["fp8_restore"] == "mapped":
+                ops.restore_fp8(pool, [block_id], [mapped_payload], [mapped_scale], stream=stream)
+            else:
+                staged, staged_scale = self._stage(stream)
+                ops.restore_fp8_staged(pool, [block_id], [payload], [scale], staged,
+                                       staged_scale, stream=stream)
+            return
+        method = modes["bf16_restore"]
+        if method == "tma":
+            staged, _ = self._stage(stream)
+            ops.memcpy(staged.data_ptr(), payload, self._payload_bytes, device=pool.device,
+                       stream=stream)
+            ops.copy_blocks(pool, [block_id], [staged.data_ptr()], restore=True,
+                            method=ops.COPY_TMA, stream=stream)
+        elif method == "sm":
+            ops.copy_blocks(pool, [block_id], [mapped_payload], restore=True,
+                            method=ops.COPY_SM, stream=stream)
+        else:
+            ops.copy_blocks(pool, [block_id], [payload], restore=True, stream=stream)
+
+    def _restore_slot(self, slot: int, block_id: int, stream):
+        mapped = self._slot_pointers(slot, True)
+        plain = self._slot_pointers(slot, False)
+        self._device_restore(self._cache, block_id, plain[0], plain[1], mapped[0], mapped[1],
+                             stream)
+
+    # -- host copies (CPU pools: the reference's synchronous path) ---------------
+
+    def _host_save(self, source: torch.Tensor, payload: torch.Tensor, scale):
+        if self._fp8:
+            fp8_quantize(source, payload, scale)
+        else:
+            payload.copy_(source)
+
+    def _host_restore(self, entry: _CPUBlock, target: torch.Tensor):
+        if self._fp8:
+            fp8_dequantize(entry.kv, entry.scale, target)
+        else:
+            target.copy_(entry.kv)
+
+    # -- engine API -------------------------------------------------------------
+
+    @torch.inference_mode()
+    def measure_restore_s_per_block(self, repeats: int = 8) -> float:
+        """Seconds per block of this cache's restore path (H2D, plus FP8 dequant)."""
+        self._require_open()
+        if not self._on_cuda:
+            raise RuntimeError("restore timing needs a CUDA KV pool")
+        from kvoff.slab import PinnedSlab
+
+        pool = self._cache
+        scratch_pool = torch.empty((2, pool.shape[1], 1, *pool.shape[3:]), dtype=pool.dtype,
+                                   device=pool.device)
+        scale_offset = -(-repeats * self._payload_bytes // 256) * 256
+        slab = PinnedSlab(scale_offset + repeats * self._scale_bytes, device=pool.device.index)
+        payload = slab.view(0, (repeats, self._payload_bytes), torch.uint8)
+        payload.zero_()
+        scale = None
+        if self._fp8:
+            scale = slab.view(scale_offset, (repeats, self._scale_bytes // 2), pool.dtype)
+            scale.fill_(1.0)
+        stream = self._restore_stream
+        stream.wait_stream(torch.cuda.current_stream(pool.device))
+        for _ in range(2):  # the first pass warms up kernels and clocks
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                start.record(stream)
+                for i in range(repeats):
+                    p, s = payload[i].data_ptr(), scale[i].data_ptr() if scale is not None else 0
+                    self._device_restore(scratch_pool, 0, p, s, slab.device_alias(payload[i]),
+                                         slab.device_alias(scale[i]) if scale is not None else 0,
+                                         stream)
+                end.record(stream)
+            end.synchronize()
+        return start.elapsed_time(end) / 1000 / repeats
+
+    def synchronize(self):
+        """Wait for every pending host<->device copy (needed before host reads)."""
+        for stream in {self._copy_stream, self._restore_stream} - {None}:
+            stream.synchronize()
+
+    @torch.inference_mode()
+    def save_block(self, prefix_hash: int) -> bool:
+        """Save a published full block; False if it is already saved.
+
+        A full budget raises CPUCacheFullError before any allocation. A failed
+        copy leaves CPU entries and GPU metadata unchanged. Partial tail blocks
+        cannot be saved.
+        """
+        self._require_open()
+        entry = self._entries.get(prefix_hash)
+        block_id = self._manager.hash_to_block_id.get(prefix_hash)
+        if block_id is None:
+            if entry is not None:
+                return False
+            raise KeyError(f"GPU prefix block {prefix_hash} is not cached")
+        block = self._manager.blocks[block_id]
+        tokens = tuple(block.token_ids)
+        if block.hash != prefix_hash or len(tokens) != self._manager.block_size:
+            raise ValueError("source must be a published full prefix block")
+        if entry is not None:
+            if entry.token_ids != tokens:
+                raise ValueError("prefix hash has conflicting token metadata")
+            return False
+        if self.bytes_used + self._block_bytes > self._max_bytes:
+            raise CPUCacheFullError("CPU prefix cache payload budget exceeded")
+        if not self._free_slots:
+            self._grow()
+        slot = self._free_slots.pop()
+        done = None
+        try:
+            payload, scale = self._slot_view(slot)
+            if self._on_cuda:
+                done = self._save_on_device(block_id, slot)
+            else:
+                self._host_save(self._cache[:, :, block_id], payload, scale)
+        except BaseException:
+            self._free_slots.append(slot)
+            raise
+        self._entries[prefix_hash] = _CPUBlock(tokens, payload, slot, scale, done)
+        self._saved_blocks += 1
+        return True
+
+    def _save_on_device(self, block_id: int, slot: int) -> torch.cuda.Event:
+        pool = self._cache
+        current = torch.cuda.current_stream(pool.device)
+        copy = self._copy_stream
+        # After the kernels that wrote the block; with split streams also after
+        # earlier restores that read this slot. before_block_reuse orders the
+        # block's next writer after the returned event.
+        copy.wait_stream(current)
+        read = self._slot_reads.pop(slot, None)
+        if read is not None and self._restore_stream is not copy:
+            copy.wait_event(read)
+        with torch.cuda.stream(copy):
+            self._device_save(pool, block_id, slot, copy)
+            done = torch.cuda.Event()
+            done.record(copy)
+        self._pending_saves[block_id] = done
+        return done
+
+    def _preserve(self, prefix_hash: int):
+        # Only a full budget is an expected, silent skip; device and copy
+        # errors propagate.
+        try:
+            self.save_block(prefix_hash)
+        except CPUCacheFullError:
+            self._budget_skips += 1
+
+    def _preserve_before_recycle(self, prefix_hash: int):
+        self._preserve(prefix_hash)
+
+    def _preserve_on_release(self, prefix_hash: int):
+        # Save eagerly only while a request waits for blocks; otherwise the
+        # block likely stays a GPU hit and the D2H traffic would only delay
+        # small per-step copies.
+        if self._save_on_release and self._manager.admission_blocked:
+            self._preserve(prefix_hash)
+
+    def before_block_reuse(self, block_id: int):
+        """Order later writes of a GPU block after its pending copies (no host sync)."""
+        for pending in (self._pending_saves, self._pending_restores):
+            done = pending.pop(block_id, None)
+            if done is not None:
+                torch.cuda.current_stream(self._cache.device).wait_event(done)
+
+    def before_block_use(self, block_id: int):
+        """Order later reads of a prefetched GPU block after its restore."""
+        done = self._pending_restores.pop(block_id, None)
+        if done is not None:
+            torch.cuda.current_stream(self._cache.device).wait_event(done)
+
+    def _entry_for(self, prefix_hash: int, token_ids):
+        """Pure lookup for admission planning; entries stay valid during copies."""
+        entry = self._entries.get(prefix_hash)
+        if entry is None or entry.token_ids != tuple(token_ids):
+            return None
+        return entry
+
+    @torch.inference_mode()
+    def _copy_entry(self, entry: _CPUBlock, block_id: int, wait: bool = True):
+        self._require_open()
+        if not self._on_cuda:
+            self._host_restore(entry, self._cache[:, :, block_id])
+            self._restored_blocks += 1
+            return
+        pool = self._cache
+        current = torch.cuda.current_stream(pool.device)
+        stream = self._restore_stream
+        # The target may still be read by queued kernels, and the slot may
+        # still be filling from its own save.
+        stream.wait_stream(current)
+        if entry.saved is not None and stream is not self._copy_stream:
+            stream.wait_event(entry.saved)
+        with torch.cuda.stream(stream):
+            self._restore_slot(entry.slot, block_id, stream)
+            done = torch.cuda.Event()
+            done.record(stream)
+        self._slot_reads[entry.slot] = done
+        if wait:
+            current.wait_event(done)
+        else:
+            self._pending_restores[block_id] = done
+        self._restored_blocks += 1
+
+    @torch.inference_mode()
+    def restore_block(self, prefix_hash: int) -> int:
+        """Restore a CPU hit; return the GPU block it now occupies.
+
+        GPU hits are reused without a copy. On copy failure the destination is
+        freed and the hash stays unpublished; the CPU entry remains for retry.
+        """
+        self._require_open()
+        entry = self._entries[prefix_hash]
+        return self._manager.restore_cached_block(
+            prefix_hash, entry.token_ids, lambda block_id: self._copy_entry(entry, block_id))
+
+    def discard(self, prefix_hash: int) -> bool:
+        """Release one CPU payload without changing GPU cache state."""
+        self._require_open()
+        entry = self._entries.pop(prefix_hash, None)
+        if entry is None:
+            return False
+        # A later save into the slot is ordered after a pending restore of it
+        # by the slot-read event (split streams) or by stream order.
+        self._free_slots.append(entry.slot)
+        return True
+
+    def clear(self):
+        self._free_slots.extend(entry.slot for entry in self._entries.values())
+        self._entries.clear()
+
+    def close(self):
+        """Release payloads and pool references; idempotent."""
+        if self.closed:
+            return
+        if self.automatic:
+            self._manager._cpu_prefix_cache = None
+        self.synchronize()
+        self.clear()
+        for table in (self._pending_saves, self._pending_restores, self._slot_reads,
+                      self._staging):
+            table.clear()
+        self._slabs.clear()
+        self._scale_slabs.clear()
+        self._slab_owners.clear()
+        self._free_slots.clear()
+        self._num_slots = 0
+        self._cache = None
+        self._manager = None

@@ -1,0 +1,228 @@
+"""Tensor-level wrappers over the libkvoff C ABI.
+
+Every function enqueues work on a CUDA stream (default: the current stream of
+the pool's device) and never synchronizes the host. Slots are addressed by raw
+pointers so that one call can target pinned host slabs, their device aliases
+(zero-copy) or device staging buffers.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from kvoff import _lib
+from kvoff._lib import COPY_ENGINE, COPY_SM, COPY_TMA  # noqa: F401  (re-exported)
+
+
+@dataclass(frozen=True)
+class PoolGeometry:
+    """Geometry of a paged pool [2, L, NB, BS, H, D] (strides in elements).
+
+    Chunk c = kv * L + layer of block b starts at c * chunk_stride +
+    b * block_stride and holds rows_per_chunk = BS * H dense rows of D.
+    """
+
+    num_chunks: int
+    chunk_stride: int
+    block_stride: int
+    num_blocks: int
+    rows_per_chunk: int
+    head_dim: int
+    elem_size: int
+
+    @property
+    def rows(self) -> int:
+        return self.num_chunks * self.rows_per_chunk
+
+    @property
+    def chunk_bytes(self) -> int:
+        return self.rows_per_chunk * self.head_dim * self.elem_size
+
+    @property
+    def block_bytes(self) -> int:
+        """Raw (BF16-mode) bytes of one block."""
+        return self.num_chunks * self.chunk_bytes
+
+    @property
+    def fp8_payload_bytes(self) -> int:
+        return self.rows * self.head_dim
+
+    @property
+    def fp8_scale_bytes(self) -> int:
+        return self.rows * 2
+
+
+def geometry(pool: torch.Tensor) -> PoolGeometry:
+    """Validate a pool's layout and return its geometry."""
+    if pool.ndim != 6 or pool.shape[0] != 2 or min(pool.shape) <= 0:
+        raise ValueError("KV pool must be a non-empty [2, L, NB, BS, H, D] tensor")
+    _, layers, num_blocks, block_size, heads, dim = pool.shape
+    s = pool.stride()
+    if s[5] != 1 or s[4] != dim or s[3] != heads * dim:
+        raise ValueError("each KV block chunk [BS, H, D] must be dense")
+    if layers > 1 and s[0] != layers * s[1]:
+        raise ValueError("(K/V, layer) chunks of the pool must be evenly strided")
+    chunk_stride = s[1] if layers > 1 else s[0]
+    return PoolGeometry(2 * layers, chunk_stride, s[2], num_blocks, block_size * heads, dim,
+                        pool.element_size())
+
+
+def _stream(device: torch.device, stream) -> int:
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    return int(stream.cuda_stream) if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{what} must be a CUDA tensor")
+
+
+def _require_bf16(pool: torch.Tensor) -> None:
+    if pool.dtype != torch.bfloat16:
+        raise ValueError("the FP8 codec quantizes bf16 KV pools")
+
+
+def save_fp8(pool: torch.Tensor, block_ids, payload_ptrs, scale_ptrs, *, stream=None,
+             max_ctas: int = 0) -> None:
+    """Quantize blocks into device-accessible slots (device staging or mapped host)."""
+    _require_cuda(pool, "pool")
+    _require_bf16(pool)
+    g = geometry(pool)
+    n = len(block_ids)
+    if len(payload_ptrs) != n or len(scale_ptrs) != n:
+        raise ValueError("one payload and scale pointer per block")
+    with torch.cuda.device(pool.device):
+        _lib.call("kvoff_fp8_save_blocks", pool.data_ptr(), g.num_chunks, g.chunk_stride,
+                  g.block_stride, g.num_blocks, g.rows_per_chunk, g.head_dim,
+                  _lib.int64_array(block_ids), n, _lib.pointer_array(payload_ptrs),
+                  _lib.pointer_array(scale_ptrs), max_ctas, _stream(pool.device, stream))
+
+
+def restore_fp8(pool: torch.Tensor, block_ids, payload_ptrs, scale_ptrs, *, stream=None,
+                max_ctas: int = 0) -> None:
+    """Dequantize device-accessible slots into pool blocks."""
+    _require_cuda(pool, "pool")
+    _require_bf16(pool)
+    g = geometry(pool)
+    n = len(block_ids)
+    if len(payload_ptrs) != n or len(scale_ptrs) != n:
+        raise ValueError("one payload and scale pointer per block")
+    with torch.cuda.device(pool.device):
+        _lib.call("kvoff_fp8_restore_blocks", pool.data_ptr(), g.num_chunks, g.chunk_stride,
+                  g.block_stride, g.num_blocks, g.rows_per_chunk, g.head_dim,
+                  _lib.int64_array(block_ids), n, _lib.pointer_array(payload_ptrs),
+                  _lib.pointer_array(scale_ptrs), max_ctas, _stream(pool.device, stream))
+
+
+def _staging_blocks(g: PoolGeometry, staging_payload: torch.Tensor,
+                    staging_scale: torch.Tensor) -> int:
+    _require_cuda(staging_payload, "staging payload")
+    _require_cuda(staging_scale, "staging scale")
+    count = min(staging_payload.numel() * staging_payload.element_size() // g.fp8_payload_bytes,
+                staging_scale.numel() * staging_scale.element_size() // g.fp8_scale_bytes)
+    if count < 1:
+        raise ValueError("staging buffers hold less than one block")
+    return count
+
+
+def save_fp8_staged(pool: torch.Tensor, block_ids, host_payload_ptrs, host_scale_ptrs,
+                    staging_payload: torch.Tensor, staging_scale: torch.Tensor, *,
+                    stream=None) -> None:
+    """Quantize into device staging, then cudaMemcpyAsync each slot to pinned host."""
+    _require_cuda(pool, "pool")
+    _require_bf16(pool)
+    g = geometry(pool)
+    n = len(block_ids)
+    if len(host_payload_ptrs) != n or len(host_scale_ptrs) != n:
+        raise ValueError("one payload and scale pointer per block")
+    staged = _staging_blocks(g, staging_payload, staging_scale)
+    with torch.cuda.device(pool.device):
+        _lib.call("kvoff_fp8_save_blocks_staged", pool.data_ptr(), g.num_chunks, g.chunk_stride,
+                  g.block_stride, g.num_blocks, g.rows_per_chunk, g.head_dim,
+                  _lib.int64_array(block_ids), n, _lib.pointer_array(host_payload_ptrs),
+                  _lib.pointer_array(host_scale_ptrs), staging_payload.data_ptr(),
+                  staging_scale.data_ptr(), staged, _stream(pool.device, stream))
+
+
+def restore_fp8_staged(pool: torch.Tensor, block_ids, host_payload_ptrs, host_scale_ptrs,
+                       staging_payload: torch.Tensor, staging_scale: torch.Tensor, *,
+                       stream=None) -> None:
+    """cudaMemcpyAsync each pinned slot into device staging, then dequantize."""
+    _require_cuda(pool, "pool")
+    _require_bf16(pool)
+    g = geometry(pool)
+    n = len(block_ids)
+    if len(host_payload_ptrs) != n or len(host_scale_ptrs) != n:
+        raise ValueError("one payload and scale pointer per block")
+    staged = _staging_blocks(g, staging_payload, staging_scale)
+    with torch.cuda.device(pool.device):
+        _lib.call("kvoff_fp8_restore_blocks_staged", pool.data_ptr(), g.num_chunks,
+                  g.chunk_stride, g.block_stride, g.num_blocks, g.rows_per_chunk, g.head_dim,
+                  _lib.int64_array(block_ids), n, _lib.pointer_array(host_payload_ptrs),
+                  _lib.pointer_array(host_scale_ptrs), staging_payload.data_ptr(),
+                  staging_scale.data_ptr(), staged, _stream(pool.device, stream))
+
+
+def copy_blocks(pool: torch.Tensor, block_ids, slot_ptrs, *, restore: bool = False,
+                method: int = COPY_ENGINE, stream=None, max_ctas: int = 0) -> None:
+    """Byte-exact block moves pool <-> dense slots (BF16 passthrough)."""
+    _require_cuda(pool, "pool")
+    g = geometry(pool)
+    e = g.elem_size
+    n = len(block_ids)
+    if len(slot_ptrs) != n:
+        raise ValueError("one slot pointer per block")
+    with torch.cuda.device(pool.device):
+        _lib.call("kvoff_copy_blocks", pool.data_ptr(), g.num_chunks, g.chunk_stride * e,
+                  g.block_stride * e, g.num_blocks, g.chunk_bytes, _lib.int64_array(block_ids), n,
+                  _lib.pointer_array(slot_ptrs), _lib.RESTORE if restore else _lib.SAVE, method,
+                  max_ctas, _stream(pool.device, stream))
+
+
+def memcpy(dst_ptr: int, src_ptr: int, nbytes: int, *, device, stream=None) -> None:
+    """cudaMemcpyAsync(cudaMemcpyDefault) on `stream`."""
+    device = torch.device(device)
+    with torch.cuda.device(device):
+        _lib.call("kvoff_memcpy", int(dst_ptr), int(src_ptr), int(nbytes), _stream(device, stream))
+
+
+def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
+                  v_cache: torch.Tensor, slot_mapping: torch.Tensor, *,
+                  bad_slots: torch.Tensor | None = None, stream=None) -> None:
+    """Write row i of key/value [N, H, D] to cache slot slot_mapping[i] (-1: skip).
+
+    Same contract as nanovllm/layers/attention.py:33-40 (including its layout
+    assertions); the scatter is one CUDA-graph-capturable kernel launch.
+    """
+    num_tokens, num_heads, head_dim = key.shape
+    row = num_heads * head_dim
+    if not (key.stride(-1) == 1 and value.stride(-1) == 1):
+        raise AssertionError("key/value last dim must be contiguous")
+    if not (key.stride(1) == head_dim and value.stride(1) == head_dim):
+        raise AssertionError("key/value heads must be dense")
+    if not (k_cache.stride(1) == row and v_cache.stride(1) == row):
+        raise AssertionError("cache slots must hold dense [H, D] rows")
+    if slot_mapping.numel() != num_tokens:
+        raise AssertionError("one slot per token")
+    if value.shape != key.shape:
+        raise ValueError("key and value shapes differ")
+    if not (key.dtype == value.dtype == k_cache.dtype == v_cache.dtype):
+        raise ValueError("key, value and caches must share a dtype")
+    if slot_mapping.dtype != torch.int32:
+        raise ValueError("slot_mapping must be int32")
+    for t, what in ((key, "key"), (value, "value"), (k_cache, "k_cache"), (v_cache, "v_cache"),
+                    (slot_mapping, "slot_mapping")):
+        _require_cuda(t, what)
+    if bad_slots is not None and (bad_slots.dtype != torch.int32 or not bad_slots.is_cuda):
+        raise ValueError("bad_slots must be a CUDA int32 tensor")
+    e = key.element_size()
+    num_slots = k_cache.numel() // row if row else 0
+    with torch.cuda.device(key.device):
+        _lib.call("kvoff_store_kvcache", key.data_ptr(), key.stride(0) * e, value.data_ptr(),
+                  value.stride(0) * e, k_cache.data_ptr(), v_cache.data_ptr(), row * e,
+                  slot_mapping.data_ptr(), num_tokens, num_slots,
+                  bad_slots.data_ptr() if bad_slots is not None else None,
+                  _stream(key.device, stream))

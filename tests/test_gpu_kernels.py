@@ -1,0 +1,263 @@
+"""CUDA kernels vs the CPU oracle, through the C ABI (tensor wrappers in kvoff.ops).
+
+FP8 payloads and scales must match bit for bit, NaN and Inf rows included;
+restored bf16 values must match bit for bit (NaN results are written as 0xFFFF
+by both). BF16 passthrough and store_kvcache are byte moves and must be
+byte-exact over arbitrary bit patterns.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import workloads
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def sha(a) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def to_bf16(bits: np.ndarray, device) -> torch.Tensor:
+    t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16)
+    return t.to(device)
+
+
+def u16(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def u8(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().cpu().view(torch.uint8).numpy()
+
+
+def special_pool(layers: int, num_blocks: int, block_size: int, heads: int, d: int,
+                 seed: int = 0) -> np.ndarray:
+    """Pool whose rows cycle through every codec branch plus random finite rows."""
+    rows = workloads.special_rows(d, seed)
+    shape = (2, layers, num_blocks, block_size, heads, d)
+    total = int(np.prod(shape[:-1]))
+    rng = np.random.default_rng([seed, 99])
+    finite = workloads.f32_to_bf16_bits(rng.standard_normal((total, d), dtype=np.float32))
+    finite[: total: 3] = np.resize(rows, (len(finite[: total: 3]), d))
+    return finite.reshape(shape)
+
+
+def empty_slots(n: int, g, device):
+    payload = torch.empty((n, g.fp8_payload_bytes), dtype=torch.uint8, device=device)
+    scale = torch.empty((n, g.fp8_scale_bytes), dtype=torch.uint8, device=device)
+    return payload, scale
+
+
+@pytest.mark.parametrize("d,heads,block_size", [(128, 8, 256), (64, 4, 64), (256, 2, 32),
+                                               (32, 3, 16), (4, 1, 256), (8, 2, 16),
+                                               (80, 2, 16)])
+def test_fp8_save_restore_bit_exact(cuda, d, heads, block_size):
+    from kvoff import ops
+
+    bits = special_pool(2, 5, block_size, heads, d)
+    pool = to_bf16(bits, cuda)
+    g = ops.geometry(pool)
+    ids = [3, 0, 4]
+    payload, scale = empty_slots(len(ids), g, cuda)
+    ops.save_fp8(pool, ids, [p.data_ptr() for p in payload], [s.data_ptr() for s in scale])
+    want_p, want_s = oracle.fp8_save_blocks(bits, ids)
+    torch.cuda.synchronize()
+    assert np.array_equal(u8(payload).reshape(want_p.shape), want_p)
+    assert np.array_equal(u16(scale.view(torch.bfloat16)).reshape(want_s.shape), want_s)
+
+    targets = [1, 2, 3]
+    ops.restore_fp8(pool, targets, [p.data_ptr() for p in payload], [s.data_ptr() for s in scale])
+    oracle.fp8_restore_blocks(bits, targets, want_p, want_s)
+    torch.cuda.synchronize()
+    assert np.array_equal(u16(pool), bits)
+
+
+def test_fp8_restore_of_arbitrary_slot_bits(cuda):
+    from kvoff import ops
+
+    rng = np.random.default_rng(4)
+    shape = (2, 2, 3, 64, 4, 128)
+    bits = rng.integers(0, 1 << 16, shape).astype(np.uint16)
+    pool = to_bf16(bits, cuda)
+    g = ops.geometry(pool)
+    p = rng.integers(0, 256, (2, g.fp8_payload_bytes)).astype(np.uint8)
+    s = rng.integers(0, 1 << 16, (2, g.rows)).astype(np.uint16)
+    dp, ds = torch.from_numpy(p).to(cuda), torch.from_numpy(s.view(np.int16)).to(cuda)
+    ops.restore_fp8(pool, [2, 0], [x.data_ptr() for x in dp], [x.data_ptr() for x in ds])
+    oracle.fp8_restore_blocks(bits, [2, 0], p.reshape(2, 2, 2, 64, 4, 128),
+                              s.reshape(2, 2, 2, 64, 4, 1))
+    torch.cuda.synchronize()
+    assert np.array_equal(u16(pool), bits)
+
+
+def test_fp8_config1_matches_reference_digests(cuda):
+    """BASELINE config 1 at full size: 16 blocks of [2, 28, 256, 8, 128]."""
+    from kvoff import ops
+
+    golden = json.loads((GOLDEN / "config1.json").read_text())
+    c = golden["config"]
+    sources, targets = golden["sources"], golden["targets"]
+    bits = workloads.pool_with_blocks(sources, c["layers"], c["num_blocks"], c["block_size"],
+                                      c["heads"], c["head_dim"], c["seed"])
+    pool = to_bf16(bits, cuda)
+    del bits
+    g = ops.geometry(pool)
+    payload, scale = empty_slots(len(sources), g, cuda)
+    ops.save_fp8(pool, sources, [p.data_ptr() for p in payload], [s.data_ptr() for s in scale])
+    assert [sha(u8(p)) for p in payload] == golden["fp8"]["payload_sha256"]
+    assert [sha(u8(s)) for s in scale] == golden["fp8"]["scale_sha256"]
+    ops.restore_fp8(pool, targets, [p.data_ptr() for p in payload], [s.data_ptr() for s in scale])
+    assert [sha(u16(pool[:, :, t])) for t in targets] == golden["fp8"]["restored_sha256"]
+
+
+def test_fp8_staged_and_mapped_pinned_slots(cuda):
+    from kvoff import ops
+    from kvoff.slab import PinnedSlab
+
+    bits = special_pool(3, 6, 256, 8, 128, seed=2)
+    pool = to_bf16(bits, cuda)
+    g = ops.geometry(pool)
+    ids = [5, 1]
+    n = len(ids)
+    slab = PinnedSlab(2 * n * (g.fp8_payload_bytes + g.fp8_scale_bytes), device=0)
+    half = n * (g.fp8_payload_bytes + g.fp8_scale_bytes)
+    views = []
+    for k in range(2):  # k=0 staged slots, k=1 mapped slots
+        base = k * half
+        payload = slab.view(base, (n, g.fp8_payload_bytes), torch.uint8)
+        scale = slab.view(base + n * g.fp8_payload_bytes, (n, g.fp8_scale_bytes), torch.uint8)
+        payload.fill_(0xAB)
+        scale.fill_(0xCD)
+        views.append((payload, scale))
+    staging_p, staging_s = empty_slots(1, g, cuda)  # one block of staging: two rounds
+    (hp, hs), (mp, ms) = views
+    ops.save_fp8_staged(pool, ids, [p.data_ptr() for p in hp], [s.data_ptr() for s in hs],
+                        staging_p, staging_s)
+    ops.save_fp8(pool, ids, [slab.device_alias(p) for p in mp], [slab.device_alias(s) for s in ms],
+                 max_ctas=64)
+    torch.cuda.synchronize()
+    want_p, want_s = oracle.fp8_save_blocks(bits, ids)
+    for payload, scale in views:
+        assert np.array_equal(payload.numpy().reshape(want_p.shape), want_p)
+        assert np.array_equal(scale.numpy().view(np.uint16).reshape(want_s.shape), want_s)
+    ops.restore_fp8_staged(pool, [0, 2], [p.data_ptr() for p in hp], [s.data_ptr() for s in hs],
+                           staging_p, staging_s)
+    ops.restore_fp8(pool, [3, 4], [slab.device_alias(p) for p in mp],
+                    [slab.device_alias(s) for s in ms])
+    oracle.fp8_restore_blocks(bits, [0, 2], want_p, want_s)
+    oracle.fp8_restore_blocks(bits, [3, 4], want_p, want_s)
+    torch.cuda.synchronize()
+    assert np.array_equal(u16(pool), bits)
+
+
+def test_fp8_batches_larger_than_one_launch(cuda):
+    from kvoff import ops
+
+    bits = special_pool(1, 140, 16, 1, 128, seed=3)
+    pool = to_bf16(bits, cuda)
+    g = ops.geometry(pool)
+    ids = list(range(139, -1, -1))[:135]
+    payload, scale = empty_slots(len(ids), g, cuda)
+    ops.save_fp8(pool, ids, [p.data_ptr() for p in payload], [s.data_ptr() for s in scale])
+    want_p, want_s = oracle.fp8_save_blocks(bits, ids)
+    torch.cuda.synchronize()
+    assert np.array_equal(u8(payload).reshape(want_p.shape), want_p)
+    assert np.array_equal(u16(scale.view(torch.bfloat16)).reshape(want_s.shape), want_s)
+
+
+@pytest.mark.parametrize("method", ["engine", "tma", "sm"])
+@pytest.mark.parametrize("shape", [(2, 3, 6, 256, 8, 128), (2, 2, 4, 256, 1, 4)])
+def test_bf16_passthrough_byte_exact(cuda, method, shape):
+    from kvoff import ops
+    from kvoff.slab import PinnedSlab
+
+    code = {"engine": ops.COPY_ENGINE, "tma": ops.COPY_TMA, "sm": ops.COPY_SM}[method]
+    rng = np.random.default_rng(len(shape) + shape[-1])
+    bits = rng.integers(0, 1 << 16, shape).astype(np.uint16)  # NaN encodings included
+    pool = to_bf16(bits, cuda)
+    g = ops.geometry(pool)
+    ids, targets = [4, 1, 2], [0, 3, 5 % shape[2]]
+    if method == "tma":  # device slots only
+        slots = torch.empty((len(ids), g.block_bytes), dtype=torch.uint8, device=cuda)
+        ptrs = [s.data_ptr() for s in slots]
+        host = None
+    else:
+        slab = PinnedSlab(len(ids) * g.block_bytes, device=0)
+        host = slab.view(0, (len(ids), g.block_bytes), torch.uint8)
+        ptrs = [slab.device_alias(s) if method == "sm" else s.data_ptr() for s in host]
+    ops.copy_blocks(pool, ids, ptrs, method=code)
+    torch.cuda.synchronize()
+    got = (slots.cpu() if host is None else host).numpy()
+    want = oracle.copy_blocks(bits, ids)
+    assert np.array_equal(got.view(np.uint16).reshape(want.shape), want)
+    ops.copy_blocks(pool, targets, ptrs, restore=True, method=code)
+    oracle.copy_blocks(bits, targets, want, restore=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(u16(pool), bits)
+    from kvoff import device_error
+    assert device_error(0) == 0
+
+
+@pytest.mark.parametrize("name", sorted(workloads.STORE_CASES))
+def test_store_kvcache_matches_oracle_and_fixture(cuda, name):
+    from kvoff import ops
+
+    golden = json.loads((GOLDEN / "store_kvcache.json").read_text())[name]
+    n, h, d, nb, bs, pad = workloads.STORE_CASES[name]
+    qkv, slots, k_in, v_in = workloads.store_kvcache_inputs(name)
+    rows = to_bf16(qkv, cuda)
+    key = rows[:, pad:pad + h * d].view(n, h, d)
+    value = rows[:, pad + h * d:].view(n, h, d)
+    k_cache, v_cache = to_bf16(k_in, cuda), to_bf16(v_in, cuda)
+    slot_mapping = torch.from_numpy(slots).to(cuda)
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda)
+    ops.store_kvcache(key, value, k_cache, v_cache, slot_mapping, bad_slots=bad)
+    assert sha(u16(k_cache)) == golden["k_cache_sha256"]
+    assert sha(u16(v_cache)) == golden["v_cache_sha256"]
+    assert int(bad.item()) == 0
+
+
+def test_store_kvcache_graph_capture_and_bad_slots(cuda):
+    from kvoff import ops
+
+    n, h, d, nb, bs = 64, 8, 128, 4, 32
+    torch.manual_seed(0)
+    key = torch.randn(n, h, d, dtype=torch.bfloat16, device=cuda)
+    value = torch.randn(n, h, d, dtype=torch.bfloat16, device=cuda)
+    k_cache = torch.zeros(nb, bs, h, d, dtype=torch.bfloat16, device=cuda)
+    v_cache = torch.zeros_like(k_cache)
+    slots = torch.full((n,), -1, dtype=torch.int32, device=cuda)
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda)
+    stream = torch.cuda.Stream(cuda)
+    stream.wait_stream(torch.cuda.current_stream(cuda))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        ops.store_kvcache(key, value, k_cache, v_cache, slots, bad_slots=bad)  # warm up
+        with torch.cuda.graph(graph, stream=stream):
+            ops.store_kvcache(key, value, k_cache, v_cache, slots, bad_slots=bad)
+    torch.cuda.current_stream(cuda).wait_stream(stream)
+    mapping = torch.randperm(nb * bs, device=cuda)[:n].to(torch.int32)
+    mapping[::5] = -1
+    mapping[7] = nb * bs + 3  # out of range: skipped and counted
+    slots.copy_(mapping)
+    graph.replay()
+    torch.cuda.synchronize()
+    valid = (mapping >= 0) & (mapping < nb * bs)
+    idx = mapping[valid].long()
+    assert torch.equal(k_cache.view(-1, h * d)[idx], key.reshape(n, -1)[valid])
+    assert torch.equal(v_cache.view(-1, h * d)[idx], value.reshape(n, -1)[valid])
+    untouched = torch.ones(nb * bs, dtype=torch.bool, device=cuda)
+    untouched[idx] = False
+    assert not k_cache.view(-1, h * d)[untouched].any()
+    assert int(bad.item()) == 1
