@@ -187,7 +187,8 @@ def test_bf16_passthrough_byte_exact(cuda, method, shape):
     bits = rng.integers(0, 1 << 16, shape).astype(np.uint16)  # NaN encodings included
     pool = to_bf16(bits, cuda)
     g = ops.geometry(pool)
-    ids, targets = [4, 1, 2], [0, 3, 5 % shape[2]]
+    nb = shape[2]
+    ids, targets = [nb - 1, 1, 2], [0, nb - 2, nb - 1]
     if method == "tma":  # device slots only
         slots = torch.empty((len(ids), g.block_bytes), dtype=torch.uint8, device=cuda)
         ptrs = [s.data_ptr() for s in slots]
