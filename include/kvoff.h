@@ -128,6 +128,30 @@ KVOFF_API int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks,
                                            void* stream);
 
 /*
+ * Staged FP8 save that allocates nothing, for callers that cannot allocate
+ * device memory while saving: an engine that gives nearly all free HBM to its
+ * KV pool at start-up has no room left for a staging buffer, and a host
+ * runtime calling this library through its C ABI may have no device allocator
+ * at all. Same result as kvoff_fp8_save_blocks_staged, but it stages through
+ * a fixed 16 MiB scratch array inside the library (held on every GPU that
+ * loads the library until the process exits) and calls no allocator. Blocks
+ * larger than the scratch are processed in pieces of whole (K/V, layer)
+ * chunks; a chunk whose payload (rounded up to 256 bytes) plus scales exceeds
+ * 16 MiB is rejected with KVOFF_EINVAL. The first call on each device looks up
+ * the scratch's device address, so make that first call before any stream
+ * capture. All calls share the one scratch array and leave their data in it:
+ * calls that may overlap on the GPU (different streams, or different host
+ * threads) race and must be serialized by the caller. No counterpart in the
+ * reference.
+ */
+KVOFF_API int kvoff_fp8_save_blocks_staged_noalloc(const void* pool, int64_t num_chunks,
+                                                   int64_t chunk_stride, int64_t block_stride,
+                                                   int64_t num_blocks, int64_t rows_per_chunk,
+                                                   int64_t head_dim, const int64_t* block_ids,
+                                                   int64_t count, void* const* host_payload,
+                                                   void* const* host_scale, void* stream);
+
+/*
  * Staged FP8 restore: copy each slot host->device into staging (two
  * cudaMemcpyAsync per block), then dequantize into the pool. Replaces
  * CPUBlockCache._dequantize's CUDA branch (cpu_prefix_cache.py:237-243).

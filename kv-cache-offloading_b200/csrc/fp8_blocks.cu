@@ -17,6 +17,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "codec.cuh"
 #include "runtime.h"
 
@@ -489,3 +491,109 @@ int kvoff_fp8_restore_blocks_staged(void* pool, int64_t num_chunks, int64_t chun
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Staged FP8 save without any allocation.
+//
+// Some callers cannot allocate device memory when a block is saved: an
+// engine that hands almost all free HBM to its KV pool at start-up leaves no
+// room for a staging buffer, and a host runtime driving this library through
+// its C ABI may have no device allocator to call. This variant stages through
+// one fixed scratch array compiled into the library instead of a buffer the
+// caller passes in. The scratch holds kNoAllocScratchBytes (16 MiB) on every
+// GPU that loads the library, until the process exits. A block larger than
+// the scratch is quantized and drained in pieces of whole (K/V, layer)
+// chunks; a single chunk's payload plus scales must fit, else the call fails.
+
+namespace kvoff {
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = 16ll << 20;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device. The host-side
+// symbol is only a stand-in; the address must come from cudaGetSymbolAddress
+// with the device current. Looked up once per device, on its first call.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  KVOFF_TRY(cuda_status(cudaGetDevice(&dev), "cudaGetDevice"));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(KVOFF_EINVAL, "kvoff_fp8_save_blocks_staged_noalloc: device %d unsupported", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    KVOFF_TRY(cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch),
+                          "cudaGetSymbolAddress (no-alloc scratch)"));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return KVOFF_OK;
+}
+
+}  // namespace
+}  // namespace kvoff
+
+extern "C" int kvoff_fp8_save_blocks_staged_noalloc(
+    const void* pool, int64_t num_chunks, int64_t chunk_stride, int64_t block_stride,
+    int64_t num_blocks, int64_t rows_per_chunk, int64_t head_dim, const int64_t* block_ids,
+    int64_t count, void* const* host_payload, void* const* host_scale, void* stream) {
+  using namespace kvoff;
+  if (injected("fp8_save_blocks_staged_noalloc")) return KVOFF_EINJECTED;
+  Args a{"fp8_save_blocks_staged_noalloc", const_cast<void*>(pool), {}, num_blocks, block_ids,
+         count};
+  KVOFF_TRY(validate(a, num_chunks, chunk_stride, block_stride, rows_per_chunk, head_dim));
+  if (count == 0) return ok();
+  if (host_payload == nullptr || host_scale == nullptr)
+    return fail(KVOFF_EINVAL, "kvoff_fp8_save_blocks_staged_noalloc: null host slot table");
+  for (int64_t i = 0; i < count; ++i)
+    if (host_payload[i] == nullptr || host_scale[i] == nullptr)
+      return fail(KVOFF_EINVAL, "kvoff_fp8_save_blocks_staged_noalloc: null host slot at %lld",
+                  (long long)i);
+  // Chunks per piece: payload (rounded up to 256 B) plus scales must fit.
+  const int64_t chunk_payload = rows_per_chunk * head_dim;
+  const int64_t chunk_scale = rows_per_chunk * 2;
+  int64_t per_piece = kNoAllocScratchBytes / (chunk_payload + chunk_scale);
+  while (per_piece > 0 &&
+         (per_piece * chunk_payload + 255) / 256 * 256 + per_piece * chunk_scale >
+             kNoAllocScratchBytes)
+    --per_piece;
+  if (per_piece < 1)
+    return fail(KVOFF_EINVAL,
+                "kvoff_fp8_save_blocks_staged_noalloc: one (K/V, layer) chunk needs %lld bytes "
+                "of scratch, more than the %lld-byte maximum",
+                (long long)((chunk_payload + 255) / 256 * 256 + chunk_scale),
+                (long long)kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  KVOFF_TRY(noalloc_scratch(&scratch));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint16_t* base = static_cast<const uint16_t*>(pool);
+  for (int64_t i = 0; i < count; ++i) {
+    for (int64_t c0 = 0; c0 < num_chunks; c0 += per_piece) {
+      const int64_t k = (num_chunks - c0) < per_piece ? (num_chunks - c0) : per_piece;
+      const int64_t payload_bytes = k * chunk_payload;
+      const int64_t scale_offset = (payload_bytes + 255) / 256 * 256;
+      Args piece = a;
+      piece.pool = const_cast<uint16_t*>(base + c0 * chunk_stride);
+      piece.block_ids = block_ids + i;
+      piece.count = 1;
+      piece.g.num_chunks = k;
+      void* pdst[1] = {scratch};
+      void* sdst[1] = {static_cast<uint8_t*>(scratch) + scale_offset};
+      KVOFF_TRY(launch<true>(piece, pdst, sdst, 0, s));
+      KVOFF_TRY(cuda_status(
+          cudaMemcpyAsync(static_cast<uint8_t*>(host_payload[i]) + c0 * chunk_payload, pdst[0],
+                          payload_bytes, cudaMemcpyDefault, s),
+          "no-alloc save payload copy"));
+      KVOFF_TRY(cuda_status(
+          cudaMemcpyAsync(static_cast<uint8_t*>(host_scale[i]) + c0 * chunk_scale, sdst[0],
+                          k * chunk_scale, cudaMemcpyDefault, s),
+          "no-alloc save scale copy"));
+    }
+  }
+  return ok();
+}
