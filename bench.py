@@ -58,6 +58,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--batch", type=int, default=128, help="blocks saved and restored per step")
+    p.add_argument("--pool-blocks", type=int, default=NUM_BLOCKS,
+                   help="GPU pool size in blocks (smaller pools are for profiler captures)")
     p.add_argument("--slab-gib", type=float, default=24.0, help="pinned host slab per GPU")
     p.add_argument("--no-sweep", action="store_true", help="skip the batch-size / mode sweep")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -65,8 +67,8 @@ def parse_args():
     args = p.parse_args()
     if args.warmup < 3:
         p.error("--warmup must be >= 3")
-    if not 1 <= args.batch <= NUM_BLOCKS // 2:
-        p.error(f"--batch must be in [1, {NUM_BLOCKS // 2}]")
+    if not 1 <= args.batch <= args.pool_blocks // 2:
+        p.error(f"--batch must be in [1, pool_blocks / 2]")
     return args
 
 
@@ -307,12 +309,12 @@ def run_ours(args) -> None:
     restore_stream = torch.cuda.Stream(device)
     timer = Timer(torch, main, world)
 
-    pool = torch.empty((2, LAYERS, NUM_BLOCKS, BLOCK_SIZE, HEADS, HEAD_DIM), dtype=torch.bfloat16,
-                       device=device)
+    pool = torch.empty((2, LAYERS, args.pool_blocks, BLOCK_SIZE, HEADS, HEAD_DIM),
+                       dtype=torch.bfloat16, device=device)
     fill_pool(pool, seed=1000 + rank)
     g = ops.geometry(pool)
     rng = np.random.default_rng(rank)
-    perm = rng.permutation(NUM_BLOCKS)
+    perm = rng.permutation(args.pool_blocks)
     save_ids = [int(i) for i in perm[:B]]
     restore_ids = [int(i) for i in perm[B:2 * B]]
 
@@ -493,6 +495,10 @@ def run_ours(args) -> None:
                     "save": rate(concurrent(save, lambda: None), batch, 1, **few)[0],
                     "restore": rate(concurrent(lambda: None, restore), batch, 1, **few)[0],
                     "duplex": rate(concurrent(save, restore), batch, 2, **few)[0]}
+            for save_m, restore_m in (("mapped", "staged"), ("staged", "mapped")):
+                save, restore = e2e_fns(batch, save_m, restore_m)
+                row[f"fp8_save_{save_m}_restore_{restore_m}"] = {
+                    "duplex": rate(concurrent(save, restore), batch, 2, **few)[0]}
             for method in ("engine", "tma", "sm"):
                 save, restore = bf16_fns(batch, method)
                 row[f"bf16_{method}"] = {
@@ -500,12 +506,15 @@ def run_ours(args) -> None:
                     "restore": rate(concurrent(lambda: None, restore), batch, 1, **few)[0],
                     "duplex": rate(concurrent(save, restore), batch, 2, **few)[0]}
             sweep[str(batch)] = row
-        best = sweep[str(B)] if str(B) in sweep else {}
-        save_mode = max(("staged", "mapped"),
-                        key=lambda m: best.get(f"fp8_{m}", {}).get("save", 0)) if best else "staged"
-        restore_mode = max(("staged", "mapped"),
-                           key=lambda m: best.get(f"fp8_{m}", {}).get("restore", 0)) if best \
-            else "staged"
+        best = sweep.get(str(B), {})
+
+        def duplex(save_m, restore_m):
+            key = f"fp8_{save_m}" if save_m == restore_m else \
+                f"fp8_save_{save_m}_restore_{restore_m}"
+            return best.get(key, {}).get("duplex", 0.0)
+        combos = [(a, b) for a in ("staged", "mapped") for b in ("staged", "mapped")]
+        save_mode, restore_mode = max(combos, key=lambda c: duplex(*c)) if best else \
+            ("staged", "staged")
     else:
         save_mode = restore_mode = "staged"
 
@@ -568,7 +577,8 @@ def run_ours(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: N(0,1) bf16 with 1% x20 outlier channels per (K/V, layer, KV head)",
-        "config": {"workload": CONFIG_NAME, "batch_blocks": B, "pool_bytes": pool.numel() * 2,
+        "config": {"workload": CONFIG_NAME, "batch_blocks": B, "pool_blocks": args.pool_blocks,
+                   "pool_bytes": pool.numel() * 2,
                    "slab_bytes": slab_bytes, "slab_pin_s": pin_s, "numa_node": slab.numa_node,
                    "l2": "inputs larger than L2 (4.8 GB of KV per step)",
                    "parallelism": f"dp{world} (independent per-GPU pools and slabs, no collective)"},

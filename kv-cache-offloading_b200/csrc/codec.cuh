@@ -14,9 +14,8 @@
 
 namespace kvoff {
 
-// bf16 bit pattern written for every NaN result. torch's own NaN encodings
-// differ between its CPU vector and scalar paths and CUDA; this is the one its
-// CPU vector path produces for fp32 -> bf16.
+// bf16 bit pattern of a NaN row scale: the one the reference quantizer writes
+// (torch's fp32 -> bf16 conversion on the CPU).
 constexpr uint32_t kBf16NaN = 0xFFFFu;
 constexpr float kFp8Max = 448.0f;   // largest finite float8_e4m3fn magnitude
 constexpr float kMinScale = 1e-30f; // clamp_min of the reference scale
@@ -60,9 +59,31 @@ __device__ __forceinline__ uint32_t scale_from_amax(uint32_t amax_bits) {
   return f32_to_bf16_rne(s);
 }
 
-// Quantize one element of a finite-scale row: e4m3(clamp(x / s, +-448)).
-__device__ __forceinline__ float quant_input(float x, float s) {
-  return fminf(fmaxf(__fdiv_rn(x, s), -kFp8Max), kFp8Max);
+// x / s for one element of a finite-scale row, ready for the saturating e4m3
+// conversion (cvt ... .satfinite maps |q| > 448 to 448 exactly as the
+// reference's clamp(-448, 448) followed by RNE does). Division-free: with
+// r = RN(1/s) (one correctly rounded reciprocal per row) and q1 = RN(x * r),
+// the residual q1 * s - x is exact in one FMA, and q1 - residual * r refines q1
+// to within half an ulp plus a hair of x / s. x / s cannot lie that close to an
+// e4m3 rounding boundary without being exactly on it (x and s carry 8
+// significant bits, e4m3 midpoints 5), and on it the refinement is exact, so the
+// e4m3 byte equals that of IEEE division; computing the residual negated keeps
+// the sign of zero quotients. Checked exhaustively against IEEE division over all
+// 929,598,054 (x, s) pairs a row can produce (oracle kvo_fast_quotient_mismatches,
+// tests/test_quotient_proof.py).
+__device__ __forceinline__ float quant_input(float x, float s, float r) {
+  const float q1 = __fmul_rn(x, r);
+  const float neg_rem = __fmaf_rn(q1, s, -x);
+  return __fmaf_rn(-neg_rem, r, q1);
+}
+
+// Two fp32 -> packed bf16 pair, round to nearest even (hardware cvt; a NaN
+// becomes the canonical 0x7FFF, the encoding CUDA's own conversion writes);
+// `lo` lands in the low half.
+__device__ __forceinline__ uint32_t f32x2_to_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // e4m3 byte of one element of a row whose scale is Inf or NaN. These rows

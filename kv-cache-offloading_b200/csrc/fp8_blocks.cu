@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <map>
 #include <mutex>
 
 #include "codec.cuh"
@@ -89,10 +90,11 @@ __device__ __forceinline__ uint2 quantize8(const uint32_t w[4], uint32_t sb) {
   uint32_t b[4];
   if (sb < 0x7F80u) {
     const float s = bf16_to_f32(sb);
+    const float r = __frcp_rn(s);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float lo = quant_input(bf16_to_f32(w[j] & 0xFFFFu), s);
-      const float hi = quant_input(bf16_to_f32(w[j] >> 16), s);
+      const float lo = quant_input(bf16_to_f32(w[j] & 0xFFFFu), s, r);
+      const float hi = quant_input(bf16_to_f32(w[j] >> 16), s, r);
       b[j] = f32x2_to_e4m3x2(lo, hi);
     }
   } else {
@@ -188,7 +190,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float2 f = e4m3x2_to_f32x2(pairs[j]);
-          out[j] = f32_to_bf16_rne(__fmul_rn(f.x, s)) | (f32_to_bf16_rne(__fmul_rn(f.y, s)) << 16);
+          out[j] = f32x2_to_bf16x2(__fmul_rn(f.x, s), __fmul_rn(f.y, s));
         }
         *reinterpret_cast<uint4*>(dst + (int64_t)r * D + li * 8) =
             make_uint4(out[0], out[1], out[2], out[3]);
@@ -215,11 +217,12 @@ __global__ void fp8_save_generic_kernel(const uint16_t* __restrict__ pool, const
     for (int64_t j = 0; j < D; ++j) amax = max(amax, (uint32_t)(src[j] & 0x7FFFu));
     const uint32_t sb = scale_from_amax(amax);
     uint8_t* dst = static_cast<uint8_t*>(t.payload[idx]) + slot_row * D;
+    const float s = bf16_to_f32(sb);
+    const float rcp = __frcp_rn(s);
     for (int64_t j = 0; j < D; ++j) {
       const uint32_t x = src[j];
-      dst[j] = (uint8_t)(sb < 0x7F80u
-                             ? f32x2_to_e4m3x2(quant_input(bf16_to_f32(x), bf16_to_f32(sb)), 0.f) & 0xFFu
-                             : special_row_byte(x, sb));
+      dst[j] = (uint8_t)(sb < 0x7F80u ? f32x2_to_e4m3x2(quant_input(bf16_to_f32(x), s, rcp), 0.f) & 0xFFu
+                                      : special_row_byte(x, sb));
     }
     static_cast<uint16_t*>(t.scale[idx])[slot_row] = (uint16_t)sb;
   }
@@ -240,7 +243,7 @@ __global__ void fp8_restore_generic_kernel(uint16_t* __restrict__ pool, const Ge
     const uint8_t* src = static_cast<const uint8_t*>(t.payload[idx]) + slot_row * D;
     const float s = bf16_to_f32(static_cast<const uint16_t*>(t.scale[idx])[slot_row]);
     for (int64_t j = 0; j < D; ++j)
-      dst[j] = (uint16_t)f32_to_bf16_rne(__fmul_rn(e4m3x2_to_f32x2(src[j]).x, s));
+      dst[j] = (uint16_t)(f32x2_to_bf16x2(__fmul_rn(e4m3x2_to_f32x2(src[j]).x, s), 0.f) & 0xFFFFu);
   }
 }
 
@@ -367,6 +370,49 @@ int launch(const Args& a, void* const* payload, void* const* scale, int32_t max_
 int64_t payload_bytes(const Geometry& g) { return g.num_chunks * g.rows_per_chunk * g.head_dim; }
 int64_t scale_bytes(const Geometry& g) { return g.num_chunks * g.rows_per_chunk * 2; }
 
+// Two-stage pipeline of the staged calls. The staging buffer is split into two
+// halves. The FP8 kernels run on an auxiliary stream owned by the library (one
+// per caller stream), and events hand each half back and forth between that
+// stream and the caller's stream, so that the kernel of one group overlaps the
+// DMA of the previous group. The ring position persists across calls on the
+// same caller stream and staging buffer, so back-to-back one-block calls
+// alternate halves and overlap too. Everything a call enqueues finishes on the
+// caller's stream, as with the serial path.
+struct Pipe {
+  cudaStream_t aux = nullptr;
+  cudaEvent_t start = nullptr, done = nullptr;
+  cudaEvent_t ready[2] = {nullptr, nullptr};
+  cudaEvent_t freed[2] = {nullptr, nullptr};
+  bool freed_recorded[2] = {false, false};
+  int next = 0;
+  const void* staging = nullptr;
+};
+
+std::mutex g_pipe_mu;
+std::map<std::pair<int, cudaStream_t>, Pipe> g_pipes;
+
+int pipe_for(cudaStream_t caller, const void* staging, Pipe** out) {
+  int dev = 0;
+  KVOFF_TRY(cuda_status(cudaGetDevice(&dev), "cudaGetDevice"));
+  Pipe& p = g_pipes[{dev, caller}];
+  if (p.aux == nullptr) {
+    KVOFF_TRY(cuda_status(cudaStreamCreateWithFlags(&p.aux, cudaStreamNonBlocking),
+                          "cudaStreamCreateWithFlags (pipeline stream)"));
+    cudaEvent_t* events[] = {&p.start, &p.done, &p.ready[0], &p.ready[1], &p.freed[0],
+                             &p.freed[1]};
+    for (cudaEvent_t* e : events)
+      KVOFF_TRY(cuda_status(cudaEventCreateWithFlags(e, cudaEventDisableTiming),
+                            "cudaEventCreateWithFlags (pipeline event)"));
+  }
+  if (p.staging != staging) {  // a new staging buffer starts a fresh ring
+    p.staging = staging;
+    p.freed_recorded[0] = p.freed_recorded[1] = false;
+    p.next = 0;
+  }
+  *out = &p;
+  return KVOFF_OK;
+}
+
 }  // namespace
 }  // namespace kvoff
 
@@ -426,24 +472,49 @@ int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks, int64_t c
                   (long long)i);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t pb = payload_bytes(a.g), sb = scale_bytes(a.g);
-  const int64_t group = staging_blocks < kMaxBatch ? staging_blocks : kMaxBatch;
+  const bool pipelined = staging_blocks >= 2;
+  const int64_t half = staging_blocks / 2;
+  const int64_t cap = pipelined ? half : staging_blocks;
+  const int64_t group = cap < kMaxBatch ? cap : kMaxBatch;
+  std::unique_lock<std::mutex> lock(g_pipe_mu, std::defer_lock);
+  Pipe* p = nullptr;
+  cudaStream_t ks = s;  // stream that runs the quantize kernels
+  if (pipelined) {
+    lock.lock();
+    KVOFF_TRY(pipe_for(s, staging_payload, &p));
+    ks = p->aux;
+    KVOFF_TRY(cuda_status(cudaEventRecord(p->start, s), "cudaEventRecord"));
+    KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, p->start, 0), "cudaStreamWaitEvent"));
+  }
   void* pdst[kMaxBatch];
   void* sdst[kMaxBatch];
   for (int64_t first = 0; first < count; first += group) {
     const int64_t n = (count - first) < group ? (count - first) : group;
+    const int h = pipelined ? p->next : 0;
     for (int64_t i = 0; i < n; ++i) {
-      pdst[i] = static_cast<uint8_t*>(staging_payload) + i * pb;
-      sdst[i] = static_cast<uint8_t*>(staging_scale) + i * sb;
+      pdst[i] = static_cast<uint8_t*>(staging_payload) + (h * half + i) * pb;
+      sdst[i] = static_cast<uint8_t*>(staging_scale) + (h * half + i) * sb;
     }
+    if (pipelined && p->freed_recorded[h])  // earlier copies out of this half are done
+      KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, p->freed[h], 0), "cudaStreamWaitEvent"));
     Args sub = a;
     sub.block_ids = block_ids + first;
     sub.count = n;
-    KVOFF_TRY(launch<true>(sub, pdst, sdst, 0, s));
+    KVOFF_TRY(launch<true>(sub, pdst, sdst, 0, ks));
+    if (pipelined) {
+      KVOFF_TRY(cuda_status(cudaEventRecord(p->ready[h], ks), "cudaEventRecord"));
+      KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p->ready[h], 0), "cudaStreamWaitEvent"));
+    }
     for (int64_t i = 0; i < n; ++i) {
       KVOFF_TRY(cuda_status(cudaMemcpyAsync(host_payload[first + i], pdst[i], pb,
                                             cudaMemcpyDefault, s), "staged save payload copy"));
       KVOFF_TRY(cuda_status(cudaMemcpyAsync(host_scale[first + i], sdst[i], sb,
                                             cudaMemcpyDefault, s), "staged save scale copy"));
+    }
+    if (pipelined) {
+      KVOFF_TRY(cuda_status(cudaEventRecord(p->freed[h], s), "cudaEventRecord"));
+      p->freed_recorded[h] = true;
+      p->next = 1 - h;
     }
   }
   return ok();
@@ -469,23 +540,53 @@ int kvoff_fp8_restore_blocks_staged(void* pool, int64_t num_chunks, int64_t chun
                   (long long)i);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t pb = payload_bytes(a.g), sb = scale_bytes(a.g);
-  const int64_t group = staging_blocks < kMaxBatch ? staging_blocks : kMaxBatch;
+  const bool pipelined = staging_blocks >= 2;
+  const int64_t half = staging_blocks / 2;
+  const int64_t cap = pipelined ? half : staging_blocks;
+  const int64_t group = cap < kMaxBatch ? cap : kMaxBatch;
+  std::unique_lock<std::mutex> lock(g_pipe_mu, std::defer_lock);
+  Pipe* p = nullptr;
+  cudaStream_t ks = s;  // stream that runs the dequantize kernels
+  if (pipelined) {
+    lock.lock();
+    KVOFF_TRY(pipe_for(s, staging_payload, &p));
+    ks = p->aux;
+    // Kernels write the pool: order them after the caller stream's earlier work.
+    KVOFF_TRY(cuda_status(cudaEventRecord(p->start, s), "cudaEventRecord"));
+    KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, p->start, 0), "cudaStreamWaitEvent"));
+  }
   void* psrc[kMaxBatch];
   void* ssrc[kMaxBatch];
   for (int64_t first = 0; first < count; first += group) {
     const int64_t n = (count - first) < group ? (count - first) : group;
+    const int h = pipelined ? p->next : 0;
+    if (pipelined && p->freed_recorded[h])  // earlier kernels reading this half are done
+      KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p->freed[h], 0), "cudaStreamWaitEvent"));
     for (int64_t i = 0; i < n; ++i) {
-      psrc[i] = static_cast<uint8_t*>(staging_payload) + i * pb;
-      ssrc[i] = static_cast<uint8_t*>(staging_scale) + i * sb;
+      psrc[i] = static_cast<uint8_t*>(staging_payload) + (h * half + i) * pb;
+      ssrc[i] = static_cast<uint8_t*>(staging_scale) + (h * half + i) * sb;
       KVOFF_TRY(cuda_status(cudaMemcpyAsync(psrc[i], host_payload[first + i], pb,
                                             cudaMemcpyDefault, s), "staged restore payload copy"));
       KVOFF_TRY(cuda_status(cudaMemcpyAsync(ssrc[i], host_scale[first + i], sb,
                                             cudaMemcpyDefault, s), "staged restore scale copy"));
     }
+    if (pipelined) {
+      KVOFF_TRY(cuda_status(cudaEventRecord(p->ready[h], s), "cudaEventRecord"));
+      KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, p->ready[h], 0), "cudaStreamWaitEvent"));
+    }
     Args sub = a;
     sub.block_ids = block_ids + first;
     sub.count = n;
-    KVOFF_TRY(launch<false>(sub, psrc, ssrc, 0, s));
+    KVOFF_TRY(launch<false>(sub, psrc, ssrc, 0, ks));
+    if (pipelined) {
+      KVOFF_TRY(cuda_status(cudaEventRecord(p->freed[h], ks), "cudaEventRecord"));
+      p->freed_recorded[h] = true;
+      p->next = 1 - h;
+    }
+  }
+  if (pipelined) {  // the caller's stream sees every pool write of this call
+    KVOFF_TRY(cuda_status(cudaEventRecord(p->done, ks), "cudaEventRecord"));
+    KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p->done, 0), "cudaStreamWaitEvent"));
   }
   return ok();
 }

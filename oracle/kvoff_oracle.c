@@ -18,9 +18,9 @@
  * tricks, so it shares no code path with the device codec. NaN encodings
  * follow what torch's CPU path produced for the reference quantizer when
  * the golden fixtures were generated (tests/golden/make_golden.py): a NaN
- * fp32 -> bf16 conversion gives 0xFFFF; x / s keeps x's NaN when x is NaN,
- * else s's NaN; Inf / Inf is the default NaN with the sign set; an e4m3 NaN
- * is 0x7F with the input's sign bit.
+ * row scale is 0xFFFF; x / s keeps x's NaN when x is NaN, else s's NaN;
+ * Inf / Inf is the default NaN with the sign set; an e4m3 NaN is 0x7F with the
+ * input's sign bit. Dequantized NaN values are 0x7FFF (see dequantize_row).
  *
  * Build: oracle/build.py (gcc -O2 -fopenmp -fno-fast-math -ffp-contract=off).
  */
@@ -135,9 +135,16 @@ static void quantize_row(const uint16_t* x, int64_t d, uint8_t* out, uint16_t* s
   }
 }
 
+/* Dequantized NaN results are written as 0x7FFF, the canonical NaN of the
+ * GPU's fp32 -> bf16 conversion (the reference's own encoding here depends on
+ * torch's code path: 0x7FC0 from its scalar CPU loop, 0xFFFF from its vector
+ * loop). */
 static void dequantize_row(const uint8_t* p, uint16_t scale, int64_t d, uint16_t* out) {
   const float s = bf16_value(scale);
-  for (int64_t j = 0; j < d; ++j) out[j] = bf16_from_f32(e4m3_value(p[j]) * s);
+  for (int64_t j = 0; j < d; ++j) {
+    const float v = e4m3_value(p[j]) * s;
+    out[j] = isnan(v) ? 0x7FFF : bf16_from_f32(v);
+  }
 }
 
 ORACLE_API void kvo_set_threads(int n) {
@@ -235,4 +242,49 @@ ORACLE_API void kvo_store_kvcache(const uint8_t* key, int64_t key_stride, const 
     memcpy(k_cache + slot * row_bytes, key + i * key_stride, (size_t)row_bytes);
     memcpy(v_cache + slot * row_bytes, value + i * value_stride, (size_t)row_bytes);
   }
+}
+
+/*
+ * Exhaustive check of the device quantizer's division-free quotient
+ * (csrc/codec.cuh quant_input): for every bf16 scale s a row can produce and
+ * every finite bf16 x with |x| <= the largest amax that yields s, compare
+ *     e4m3(clamp(x / s))                                   (IEEE division)
+ *     e4m3(clamp(fma(-fma(q1, s, -x), r, q1)))            (r = 1/s, q1 = x*r)
+ * Returns the number of pairs whose e4m3 bytes differ; *pairs gets the count
+ * of pairs checked. Uses only IEEE fp32 operations, which the GPU performs
+ * identically (__frcp_rn, __fmul_rn, __fmaf_rn; denormals preserved).
+ */
+ORACLE_API int64_t kvo_fast_quotient_mismatches(int64_t* pairs) {
+  static uint16_t max_amax[65536];
+  static unsigned char seen[65536];
+  memset(max_amax, 0, sizeof max_amax);
+  memset(seen, 0, sizeof seen);
+  for (uint32_t ab = 0; ab < 0x7F80; ++ab) {
+    float s32 = bf16_value((uint16_t)ab) / 448.0f;
+    if (s32 < 1e-30f) s32 = 1e-30f;
+    const uint16_t sb = bf16_from_f32(s32);
+    seen[sb] = 1;
+    if (ab > max_amax[sb]) max_amax[sb] = (uint16_t)ab;
+  }
+  int64_t bad = 0, checked = 0;
+#pragma omp parallel for schedule(dynamic, 64) reduction(+ : bad, checked)
+  for (int32_t sb = 0; sb < 0x7F80; ++sb) {
+    if (!seen[sb]) continue;
+    const float s = bf16_value((uint16_t)sb), r = 1.0f / s;
+    const float amax = bf16_value(max_amax[sb]);
+    for (uint32_t xb = 0; xb < 65536; ++xb) {
+      if ((xb & 0x7F80) == 0x7F80) continue;
+      const float x = bf16_value((uint16_t)xb);
+      if (fabsf(x) > amax) continue;
+      ++checked;
+      float q = x / s;
+      q = q < -448.0f ? -448.0f : (q > 448.0f ? 448.0f : q);
+      const float q1 = x * r;
+      float f = fmaf(-fmaf(q1, s, -x), r, q1);
+      f = f < -448.0f ? -448.0f : (f > 448.0f ? 448.0f : f);
+      if (f32_to_bits(q) != f32_to_bits(f) && e4m3_from_f32(q) != e4m3_from_f32(f)) ++bad;
+    }
+  }
+  if (pairs != NULL) *pairs = checked;
+  return bad;
 }

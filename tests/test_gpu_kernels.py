@@ -161,6 +161,41 @@ def test_fp8_staged_and_mapped_pinned_slots(cuda):
     assert np.array_equal(u16(pool), bits)
 
 
+def test_fp8_staged_pipeline_over_many_groups_and_calls(cuda):
+    """Staging of 4 blocks runs as a two-half pipeline (kernels on a library stream)."""
+    from kvoff import ops
+    from kvoff.slab import PinnedSlab
+
+    bits = special_pool(2, 12, 128, 8, 128, seed=6)
+    pool = to_bf16(bits, cuda)
+    g = ops.geometry(pool)
+    per = g.fp8_payload_bytes + g.fp8_scale_bytes
+    slab = PinnedSlab(7 * per, device=0)
+    payload = [slab.view(i * g.fp8_payload_bytes, (g.fp8_payload_bytes,), torch.uint8)
+               for i in range(7)]
+    scale = [slab.view(7 * g.fp8_payload_bytes + i * g.fp8_scale_bytes, (g.fp8_scale_bytes,),
+                       torch.uint8) for i in range(7)]
+    staging = empty_slots(4, g, cuda)
+    stream = torch.cuda.Stream(cuda)
+    ids = [11, 3, 7, 0, 5, 9, 1]
+    want_p, want_s = oracle.fp8_save_blocks(bits, ids)
+    for chunk in ([0, 1, 2, 3, 4], [5], [6]):  # one multi-group call, then two one-block calls
+        ops.save_fp8_staged(pool, [ids[i] for i in chunk], [payload[i].data_ptr() for i in chunk],
+                            [scale[i].data_ptr() for i in chunk], *staging, stream=stream)
+    stream.synchronize()
+    for i in range(7):
+        assert np.array_equal(payload[i].numpy(), want_p[i].reshape(-1))
+        assert np.array_equal(scale[i].numpy().view(np.uint16), want_s[i].reshape(-1))
+    targets = [2, 4, 6, 8, 10, 11, 3]
+    for chunk in ([0, 1, 2], [3, 4, 5, 6]):
+        ops.restore_fp8_staged(pool, [targets[i] for i in chunk],
+                               [payload[i].data_ptr() for i in chunk],
+                               [scale[i].data_ptr() for i in chunk], *staging, stream=stream)
+    oracle.fp8_restore_blocks(bits, targets, want_p, want_s)
+    stream.synchronize()
+    assert np.array_equal(u16(pool), bits)
+
+
 def test_fp8_batches_larger_than_one_launch(cuda):
     from kvoff import ops
 
