@@ -19,6 +19,10 @@ namespace kvoff {
 constexpr uint32_t kBf16NaN = 0xFFFFu;
 constexpr float kFp8Max = 448.0f;   // largest finite float8_e4m3fn magnitude
 constexpr float kMinScale = 1e-30f; // clamp_min of the reference scale
+// RN(1/448). bf16_rne(max(amax * kInvFp8Max, 1e-30)) equals the reference's
+// bf16_rne(max(amax / 448, 1e-30)) for every finite bf16 amax (all 32,640 are
+// checked by oracle kvo_fast_quotient_mismatches).
+constexpr float kInvFp8Max = 1.0f / 448.0f;
 
 __device__ __forceinline__ float bf16_to_f32(uint32_t bits16) {
   return __uint_as_float(bits16 << 16);
@@ -54,8 +58,7 @@ __device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t pair) {
 __device__ __forceinline__ uint32_t scale_from_amax(uint32_t amax_bits) {
   if (amax_bits > 0x7F80u) return kBf16NaN;  // a NaN in the row
   if (amax_bits == 0x7F80u) return 0x7F80u;  // +Inf amax -> +Inf scale
-  float s = __fdiv_rn(bf16_to_f32(amax_bits), kFp8Max);
-  s = fmaxf(s, kMinScale);
+  const float s = fmaxf(__fmul_rn(bf16_to_f32(amax_bits), kInvFp8Max), kMinScale);
   return f32_to_bf16_rne(s);
 }
 

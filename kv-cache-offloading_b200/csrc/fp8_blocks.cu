@@ -86,11 +86,9 @@ __device__ __forceinline__ uint2 ld_stream8(const void* p) {
 }
 
 // Quantize 8 bf16 (four packed words) of a row with scale bits `sb`.
-__device__ __forceinline__ uint2 quantize8(const uint32_t w[4], uint32_t sb) {
+__device__ __forceinline__ uint2 quantize8(const uint32_t w[4], uint32_t sb, float s, float r) {
   uint32_t b[4];
   if (sb < 0x7F80u) {
-    const float s = bf16_to_f32(sb);
-    const float r = __frcp_rn(s);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float lo = quant_input(bf16_to_f32(w[j] & 0xFFFFu), s, r);
@@ -105,43 +103,63 @@ __device__ __forceinline__ uint2 quantize8(const uint32_t w[4], uint32_t sb) {
   return make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
 }
 
+// Packed |bf16| maximum of one 16-byte vector.
+__device__ __forceinline__ uint32_t abs_max8(const uint4 v) {
+  return __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
+                  __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
+}
+
+// LANES lanes own one row of D = 16 * LANES elements; lane li handles the two
+// 8-element pieces at li * 8 and D / 2 + li * 8, so each warp-wide 16-byte load
+// and 8-byte store covers contiguous bytes of a row. kRowGroups row groups are
+// loaded before any is used (4 independent 16-byte loads per lane in flight).
 template <int LANES>
 __global__ void __launch_bounds__(kThreads)
     fp8_save_kernel(const uint16_t* __restrict__ pool, const Geometry g,
                     const __grid_constant__ BlockTable t, int64_t units) {
   constexpr int kRowsPerWarp = 32 / LANES;
   constexpr int kRowsPerIter = kRowsPerWarp * kWarps;
+  constexpr int kRowGroups = 2;
+  constexpr int D = 16 * LANES;
   __shared__ uint16_t s_scale[kTile];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int sub = lane / LANES;
   const int li = lane % LANES;
-  const int D = 8 * LANES;
 
   for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
     const Unit un = decode_unit(u, g, t);
     const uint16_t* src = pool + un.pool_elem;
     uint8_t* dst = static_cast<uint8_t*>(t.payload[un.idx]) + un.slot_row * D;
-    for (int base = 0; base < un.rows; base += kRowsPerIter * kUnroll) {
-      uint4 v[kUnroll];
+    for (int base = 0; base < un.rows; base += kRowsPerIter * kRowGroups) {
+      uint4 v[kRowGroups][2];
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
+      for (int k = 0; k < kRowGroups; ++k) {
         const int r = base + k * kRowsPerIter + warp * kRowsPerWarp + sub;
-        v[k] = r < un.rows ? ld_stream16(src + (int64_t)r * D + li * 8) : make_uint4(0, 0, 0, 0);
+        if (r < un.rows) {
+          const uint16_t* row = src + (int64_t)r * D + li * 8;
+          v[k][0] = ld_stream16(row);
+          v[k][1] = ld_stream16(row + D / 2);
+        } else {
+          v[k][0] = v[k][1] = make_uint4(0, 0, 0, 0);
+        }
       }
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
+      for (int k = 0; k < kRowGroups; ++k) {
         const int r = base + k * kRowsPerIter + warp * kRowsPerWarp + sub;
-        const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-        const uint32_t m = __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
-                                    __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
-        uint32_t amax = max(m & 0xFFFFu, m >> 16);
+        uint32_t m = __vmaxu2(abs_max8(v[k][0]), abs_max8(v[k][1]));
 #pragma unroll
         for (int off = LANES / 2; off > 0; off >>= 1)
-          amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
-        const uint32_t sb = scale_from_amax(amax);
+          m = __vmaxu2(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+        const uint32_t sb = scale_from_amax(max(m & 0xFFFFu, m >> 16));
+        const float s = bf16_to_f32(sb);
+        const float rcp = __frcp_rn(s);
         if (r < un.rows) {
-          *reinterpret_cast<uint2*>(dst + (int64_t)r * D + li * 8) = quantize8(w, sb);
+          uint8_t* out = dst + (int64_t)r * D + li * 8;
+          const uint32_t w0[4] = {v[k][0].x, v[k][0].y, v[k][0].z, v[k][0].w};
+          const uint32_t w1[4] = {v[k][1].x, v[k][1].y, v[k][1].z, v[k][1].w};
+          *reinterpret_cast<uint2*>(out) = quantize8(w0, sb, s, rcp);
+          *reinterpret_cast<uint2*>(out + D / 2) = quantize8(w1, sb, s, rcp);
           if (li == 0) s_scale[r] = (uint16_t)sb;
         }
       }
@@ -282,8 +300,9 @@ int validate(Args& a, int64_t num_chunks, int64_t chunk_stride, int64_t block_st
 
 bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
 
-// Lanes per row for the vectorized kernels, or 0 for the generic path.
-int vector_lanes(const Args& a, void* const* payload, void* const* scale) {
+// Lanes per row for the vectorized kernels, or 0 for the generic path. A save
+// lane handles 16 elements of a row, a restore lane 8.
+int vector_lanes(const Args& a, void* const* payload, void* const* scale, bool save) {
   int lanes = 0;
   switch (a.g.head_dim) {
     case 32: lanes = 4; break;
@@ -292,6 +311,7 @@ int vector_lanes(const Args& a, void* const* payload, void* const* scale) {
     case 256: lanes = 32; break;
     default: return 0;
   }
+  if (save) lanes /= 2;
   if (!aligned(a.pool, 16) || (a.g.chunk_stride % 8) != 0 || (a.g.block_stride % 8) != 0)
     return 0;
   for (int64_t i = 0; i < a.count; ++i)
@@ -303,10 +323,10 @@ template <bool kSave>
 const void* pick_kernel(int lanes) {
   if (kSave) {
     switch (lanes) {
+      case 2: return (const void*)fp8_save_kernel<2>;
       case 4: return (const void*)fp8_save_kernel<4>;
       case 8: return (const void*)fp8_save_kernel<8>;
       case 16: return (const void*)fp8_save_kernel<16>;
-      case 32: return (const void*)fp8_save_kernel<32>;
       default: return (const void*)fp8_save_generic_kernel;
     }
   }
@@ -326,7 +346,7 @@ int launch(const Args& a, void* const* payload, void* const* scale, int32_t max_
   for (int64_t i = 0; i < a.count; ++i)
     if (payload[i] == nullptr || scale[i] == nullptr)
       return fail(KVOFF_EINVAL, "kvoff_%s: null slot pointer at %lld", a.op, (long long)i);
-  const int lanes = vector_lanes(a, payload, scale);
+  const int lanes = vector_lanes(a, payload, scale, kSave);
   const void* kernel = pick_kernel<kSave>(lanes);
   for (int64_t first = 0; first < a.count; first += kMaxBatch) {
     const int n = (int)((a.count - first) < kMaxBatch ? (a.count - first) : kMaxBatch);
@@ -341,10 +361,10 @@ int launch(const Args& a, void* const* payload, void* const* scale, int32_t max_
       const int64_t grid = grid_for(units, kernel, kThreads, 0, max_ctas);
       if (kSave) {
         switch (lanes) {
+          case 2: fp8_save_kernel<2><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
           case 4: fp8_save_kernel<4><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
           case 8: fp8_save_kernel<8><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
-          case 16: fp8_save_kernel<16><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
-          default: fp8_save_kernel<32><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
+          default: fp8_save_kernel<16><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
         }
       } else {
         switch (lanes) {

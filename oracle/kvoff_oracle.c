@@ -288,3 +288,22 @@ ORACLE_API int64_t kvo_fast_quotient_mismatches(int64_t* pairs) {
   if (pairs != NULL) *pairs = checked;
   return bad;
 }
+
+/*
+ * Exhaustive check of the device quantizer's scale (csrc/codec.cuh
+ * scale_from_amax): for every finite non-negative bf16 amax, compare
+ * bf16(max(amax * RN(1/448), 1e-30)) with the reference's
+ * bf16(max(amax / 448, 1e-30)). Returns the number of differing scales.
+ */
+ORACLE_API int32_t kvo_scale_multiply_mismatches(void) {
+  const float inv = 1.0f / 448.0f;
+  int32_t bad = 0;
+  for (uint32_t ab = 0; ab < 0x7F80; ++ab) {
+    const float a = bf16_value((uint16_t)ab);
+    float div = a / 448.0f, mul = a * inv;
+    if (div < 1e-30f) div = 1e-30f;
+    if (mul < 1e-30f) mul = 1e-30f;
+    if (bf16_from_f32(div) != bf16_from_f32(mul)) ++bad;
+  }
+  return bad;
+}
