@@ -44,6 +44,10 @@ FP8_PAYLOAD = ROWS * HEAD_DIM             # 18,874,368 B
 FP8_SCALE = ROWS * 2                      # 294,912 B
 FP8_BLOCK = FP8_PAYLOAD + FP8_SCALE       # 19,169,280 B
 KERNEL_BYTES = BF16_BLOCK + FP8_BLOCK     # HBM bytes one save or restore kernel moves per block
+# dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of the save
+# kernel on 8 config-2 blocks (profiles/fp8_save_kernel_config2.md), per block;
+# traffic scales with blocks because every block is read once and written once.
+SAVE_KERNEL_DRAM_BYTES_PER_BLOCK = (302_010_880 + 103_050_240) // 8
 SWEEP_BATCHES = (1, 8, 32, 128)
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "KV restore+save GB/s (FP8, bf16-equivalent bytes)"
@@ -331,10 +335,10 @@ def run_ours(args) -> None:
     pin_s = time.perf_counter() - t0
     fp8_base, bf16_base = 0, 2 * B * FP8_BLOCK
 
-    def fp8_slot(i):  # (payload tensor, scale tensor) of FP8 slot i
-        off = fp8_base + i * FP8_BLOCK
-        return (slab.view(off, (FP8_PAYLOAD,), torch.uint8),
-                slab.view(off + FP8_PAYLOAD, (FP8_SCALE,), torch.uint8))
+    def fp8_slot(i):  # (payload, scale) of FP8 slot i: payloads first, then scales
+        return (slab.view(fp8_base + i * FP8_PAYLOAD, (FP8_PAYLOAD,), torch.uint8),
+                slab.view(fp8_base + 2 * B * FP8_PAYLOAD + i * FP8_SCALE, (FP8_SCALE,),
+                          torch.uint8))
 
     save_slots = [fp8_slot(i) for i in range(B)]
     restore_slots = [fp8_slot(B + i) for i in range(B)]
@@ -408,14 +412,7 @@ def run_ours(args) -> None:
     blocks_per_launch = B / launches_per_call
     achieved = blocks_per_launch * KERNEL_BYTES / (save_launch_ms / 1e3) / 1e9
     restore_achieved = blocks_per_launch * KERNEL_BYTES / (restore_ms / launches_per_call / 1e3) / 1e9
-    traffic = None
-    traffic_file = ROOT / "profiles" / "traffic.json"
-    if traffic_file.exists():
-        try:
-            per_block = json.loads(traffic_file.read_text())["fp8_save_kernel"]["dram_bytes_per_block"]
-            traffic = per_block * blocks_per_launch
-        except (ValueError, KeyError):
-            traffic = None
+    traffic = SAVE_KERNEL_DRAM_BYTES_PER_BLOCK * blocks_per_launch
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                 "frac": achieved / hbm_peak, "traffic": traffic,
                 "kernel": "fp8_save_kernel (gather + quantize, 128 blocks per launch)",
@@ -541,9 +538,19 @@ def run_ours(args) -> None:
         ms = timer.run(step, 5, 3) / 5
         return directions * n_bytes / (ms / 1e3) / 1e9
 
+    per_block = n_bytes // FP8_BLOCK
+
+    def chunked(copy, dst, src):
+        return lambda: [copy(dst[k * FP8_BLOCK:(k + 1) * FP8_BLOCK],
+                             src[k * FP8_BLOCK:(k + 1) * FP8_BLOCK]) for k in range(per_block)]
+
+    cp = lambda d, s_: d.copy_(s_, non_blocking=True)  # noqa: E731
     ceiling = {"d2h": memcpy_rate(concurrent(d2h, lambda: None), 1),
                "h2d": memcpy_rate(concurrent(lambda: None, h2d), 1),
                "duplex_total": memcpy_rate(concurrent(d2h, h2d), 2),
+               "duplex_total_block_copies": memcpy_rate(
+                   concurrent(chunked(cp, h_d2h, dev_buf[:n_bytes]),
+                              chunked(cp, dev_buf[n_bytes:], h_h2d)), 2),
                "bytes_per_copy": n_bytes}
     pcie_per_dir = B * FP8_BLOCK / (e2e_ms / 1e3) / 1e9
 

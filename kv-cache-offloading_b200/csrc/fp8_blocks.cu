@@ -390,6 +390,24 @@ int launch(const Args& a, void* const* payload, void* const* scale, int32_t max_
 int64_t payload_bytes(const Geometry& g) { return g.num_chunks * g.rows_per_chunk * g.head_dim; }
 int64_t scale_bytes(const Geometry& g) { return g.num_chunks * g.rows_per_chunk * 2; }
 
+// Copies dst[i] <- src[i] of `bytes` each, for i < n, merged into one
+// cudaMemcpyAsync per run of blocks that are adjacent on both sides (slots of
+// a slab are consecutive, and so is the staging), so a group of blocks drains
+// with a handful of DMA operations instead of one per block.
+int copy_runs(void* const* dst, void* const* src, int64_t n, int64_t bytes, cudaStream_t s,
+              const char* what) {
+  for (int64_t i = 0; i < n;) {
+    int64_t j = i + 1;
+    while (j < n && static_cast<uint8_t*>(dst[j]) == static_cast<uint8_t*>(dst[j - 1]) + bytes &&
+           static_cast<uint8_t*>(src[j]) == static_cast<uint8_t*>(src[j - 1]) + bytes)
+      ++j;
+    KVOFF_TRY(cuda_status(cudaMemcpyAsync(dst[i], src[i], (j - i) * bytes, cudaMemcpyDefault, s),
+                          what));
+    i = j;
+  }
+  return KVOFF_OK;
+}
+
 // Two-stage pipeline of the staged calls. The staging buffer is split into two
 // halves. The FP8 kernels run on an auxiliary stream owned by the library (one
 // per caller stream), and events hand each half back and forth between that
@@ -525,12 +543,8 @@ int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks, int64_t c
       KVOFF_TRY(cuda_status(cudaEventRecord(p->ready[h], ks), "cudaEventRecord"));
       KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p->ready[h], 0), "cudaStreamWaitEvent"));
     }
-    for (int64_t i = 0; i < n; ++i) {
-      KVOFF_TRY(cuda_status(cudaMemcpyAsync(host_payload[first + i], pdst[i], pb,
-                                            cudaMemcpyDefault, s), "staged save payload copy"));
-      KVOFF_TRY(cuda_status(cudaMemcpyAsync(host_scale[first + i], sdst[i], sb,
-                                            cudaMemcpyDefault, s), "staged save scale copy"));
-    }
+    KVOFF_TRY(copy_runs(host_payload + first, pdst, n, pb, s, "staged save payload copy"));
+    KVOFF_TRY(copy_runs(host_scale + first, sdst, n, sb, s, "staged save scale copy"));
     if (pipelined) {
       KVOFF_TRY(cuda_status(cudaEventRecord(p->freed[h], s), "cudaEventRecord"));
       p->freed_recorded[h] = true;
@@ -585,11 +599,11 @@ int kvoff_fp8_restore_blocks_staged(void* pool, int64_t num_chunks, int64_t chun
     for (int64_t i = 0; i < n; ++i) {
       psrc[i] = static_cast<uint8_t*>(staging_payload) + (h * half + i) * pb;
       ssrc[i] = static_cast<uint8_t*>(staging_scale) + (h * half + i) * sb;
-      KVOFF_TRY(cuda_status(cudaMemcpyAsync(psrc[i], host_payload[first + i], pb,
-                                            cudaMemcpyDefault, s), "staged restore payload copy"));
-      KVOFF_TRY(cuda_status(cudaMemcpyAsync(ssrc[i], host_scale[first + i], sb,
-                                            cudaMemcpyDefault, s), "staged restore scale copy"));
     }
+    KVOFF_TRY(copy_runs(psrc, const_cast<void* const*>(host_payload) + first, n, pb, s,
+                        "staged restore payload copy"));
+    KVOFF_TRY(copy_runs(ssrc, const_cast<void* const*>(host_scale) + first, n, sb, s,
+                        "staged restore scale copy"));
     if (pipelined) {
       KVOFF_TRY(cuda_status(cudaEventRecord(p->ready[h], s), "cudaEventRecord"));
       KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, p->ready[h], 0), "cudaStreamWaitEvent"));

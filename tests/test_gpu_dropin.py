@@ -1,0 +1,246 @@
+"""The drop-in CPUBlockCache on a CUDA pool (native copy path), reference-style.
+
+Restates the reference's CUDA scenarios (bench/test_cpu_prefix_cache.py,
+bench/test_cpu_cache_optimizations.py, bench/test_automatic_cpu_cache.py):
+byte-exact BF16 round trips of arbitrary bit patterns for every copy method,
+FP8 slots bit-exact against the oracle for both FP8 methods, and the stream
+ordering races provoked by delaying copies with a bounded torch.cuda._sleep on
+the cache's own streams (slabs poisoned with 0xAB so an early read shows).
+Failures are injected on the host through kvoff_debug_fail_next.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import kvoff
+from fake_engine import FakeEngine, bits_u16, block_bytes
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+SLEEP_CYCLES = 20_000_000  # about 10 ms at B200 clocks
+
+
+def arbitrary_pool(shape, device) -> torch.Tensor:
+    n = int(np.prod(shape))
+    raw = torch.arange(2 * n, dtype=torch.int64).remainder(251).to(torch.uint8)
+    return raw.view(torch.bfloat16).reshape(shape).to(device)
+
+
+def finite_pool(shape, device, seed=0) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(shape, generator=g)
+    x[..., 3] *= 20  # an outlier channel
+    return x.to(torch.bfloat16).to(device)
+
+
+def per_block(pool) -> int:
+    return pool[:, :, 0].numel() * pool.element_size()
+
+
+def slow_copies(cache, names=("save_block", "_copy_entry")):
+    """Enqueue a bounded spin on the cache's copy streams before each call."""
+    streams = {"save_block": cache._copy_stream, "_copy_entry": cache._restore_stream}
+    for name in names:
+        original, stream = getattr(cache, name), streams[name]
+
+        def delayed(*args, _original=original, _stream=stream, **kwargs):
+            with torch.cuda.stream(_stream):
+                torch.cuda._sleep(SLEEP_CYCLES)
+            return _original(*args, **kwargs)
+
+        setattr(cache, name, delayed)
+
+
+SHAPES = [(2, 2, 4, 256, 1, 4), (2, 3, 6, 256, 8, 128)]
+
+
+@pytest.mark.parametrize("method", ["engine", "tma", "sm"])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_bf16_round_trip_byte_exact(cuda, monkeypatch, method, shape):
+    monkeypatch.setenv("KVOFF_BF16_SAVE", method)
+    monkeypatch.setenv("KVOFF_BF16_RESTORE", method)
+    engine = FakeEngine(arbitrary_pool(shape, cuda))
+    m = engine.manager
+    key = m.publish(1)
+    expected = block_bytes(engine.pool, 1)
+    cache = engine.create_cpu_prefix_cache(2 * per_block(engine.pool), split_streams=True)
+    assert cache.save_block(key)
+    m.forget(key)
+    engine.pool.fill_(-7)
+    target = cache.restore_block(key)
+    cache.synchronize()
+    assert torch.equal(block_bytes(engine.pool, target), expected)
+    payload, _ = cache._slot_view(cache._entries[key].slot)
+    assert torch.equal(payload.view(torch.uint8).reshape(-1), expected.reshape(-1))
+
+
+@pytest.mark.parametrize("mode", ["staged", "mapped"])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_fp8_slots_bit_exact_and_within_bound(cuda, monkeypatch, mode, shape):
+    monkeypatch.setenv("KVOFF_FP8_SAVE", mode)
+    monkeypatch.setenv("KVOFF_FP8_RESTORE", mode)
+    engine = FakeEngine(finite_pool(shape, cuda))
+    m = engine.manager
+    keys = [m.publish(b) for b in (2, 0)]
+    pool = engine.pool
+    source = bits_u16(pool)
+    cache = engine.create_cpu_prefix_cache(4 * per_block(pool), fp8=True, split_streams=True)
+    numel = pool[:, :, 0].numel()
+    assert cache.block_bytes == numel + numel // pool.shape[-1] * pool.element_size()
+    for key in keys:
+        assert cache.save_block(key)
+    cache.synchronize()
+    want_p, want_s = oracle.fp8_save_blocks(source, [2, 0])
+    for i, key in enumerate(keys):
+        entry = cache._entries[key]
+        assert np.array_equal(entry.kv.view(torch.uint8).numpy(), want_p[i])
+        assert np.array_equal(bits_u16(entry.scale), want_s[i])
+    for key in keys:
+        m.forget(key)
+    m.free_block_ids.rotate(-3)  # restore into blocks 3 and 4
+    targets = [cache.restore_block(k) for k in keys]
+    cache.synchronize()
+    oracle.fp8_restore_blocks(source, targets, want_p, want_s)
+    assert np.array_equal(bits_u16(pool), source)
+    src = pool[:, :, 0].float()
+    back = pool[:, :, targets[1]].float()
+    assert torch.all((back - src).abs() <= src.abs().amax(-1, keepdim=True) / 16)
+    assert cache.stats["restored_blocks"] == 2
+
+
+def split_stream_cache(pool, fp8=False):
+    engine = FakeEngine(pool)
+    key = engine.manager.publish(1)
+    cache = engine.create_cpu_prefix_cache(per_block(engine.pool), split_streams=True,
+                                           preallocate=True, fp8=fp8)
+    assert cache._restore_stream is not cache._copy_stream
+    for slab in cache._slabs:
+        slab.view(torch.uint8).fill_(0xAB)  # an early read cannot see matching bytes
+    return engine, key, cache
+
+
+@pytest.mark.parametrize("slow", [False, True])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_restore_waits_for_its_save(cuda, slow, fp8):
+    engine, key, cache = split_stream_cache(finite_pool(SHAPES[1], cuda), fp8)
+    if slow:
+        slow_copies(cache, ["save_block"])  # a restore that ignored the save would overtake it
+    source = bits_u16(engine.pool)
+    expected = block_bytes(engine.pool, 1)
+    assert cache.save_block(key)
+    engine.manager.forget(key)
+    target = cache.restore_block(key)
+    cache.synchronize()
+    if fp8:
+        p, s = oracle.fp8_save_blocks(source, [1])
+        oracle.fp8_restore_blocks(source, [target], p, s)
+        assert np.array_equal(bits_u16(engine.pool[:, :, target]), source[:, :, target])
+    else:
+        assert torch.equal(block_bytes(engine.pool, target), expected)
+
+
+@pytest.mark.parametrize("slow", [False, True])
+def test_slot_reuse_waits_for_pending_restore(cuda, slow):
+    engine, key, cache = split_stream_cache(arbitrary_pool(SHAPES[1], cuda))
+    m = engine.manager
+    expected = block_bytes(engine.pool, 1)
+    assert cache.save_block(key)
+    cache.synchronize()
+    m.forget(key)
+    if slow:
+        slow_copies(cache, ["_copy_entry"])  # a fast save would overwrite the slot first
+    entry = cache._entries[key]
+    target = m.restore_cached_block(key, entry.token_ids,
+                                    lambda b: cache._copy_entry(entry, b, wait=False))
+    assert cache.discard(key)
+    other = next(i for i in range(len(m.blocks)) if i != target)
+    engine.pool[:, :, other].fill_(7)
+    other_key = m.publish(other)
+    assert cache.save_block(other_key)  # reuses the slot the restore is still reading
+    cache.synchronize()
+    cache.before_block_use(target)
+    assert torch.equal(block_bytes(engine.pool, target), expected)
+    payload, _ = cache._slot_view(0)
+    assert torch.equal(payload.view(torch.uint8).reshape(-1),
+                       block_bytes(engine.pool, other).reshape(-1))
+
+
+def test_block_reuse_waits_for_pending_save(cuda):
+    """A recycled block is rewritten only after its save finished (before_block_reuse)."""
+    engine = FakeEngine(arbitrary_pool(SHAPES[1], cuda))
+    m = engine.manager
+    key = m.publish(0)  # block 0 is first in the free list: the next allocation recycles it
+    expected = block_bytes(engine.pool, 0)
+    cache = engine.create_cpu_prefix_cache(per_block(engine.pool), automatic=True,
+                                           split_streams=True)
+    slow_copies(cache, ["save_block"])
+    block = m.allocate_block()  # preserve-before-recycle saves it, then orders reuse
+    assert block == 0 and key in cache
+    engine.pool[:, :, block].fill_(3)  # the compute stream's next write of the block
+    cache.synchronize()
+    payload, _ = cache._slot_view(cache._entries[key].slot)
+    assert torch.equal(payload.view(torch.uint8).reshape(-1), expected.reshape(-1))
+
+
+def test_injected_failures_roll_back_and_retry_is_byte_exact(cuda):
+    engine = FakeEngine(arbitrary_pool(SHAPES[1], cuda))
+    m = engine.manager
+    key = m.publish(1)
+    cache = engine.create_cpu_prefix_cache(per_block(engine.pool))
+    expected = block_bytes(engine.pool, 1)
+    kvoff.debug_fail_next("copy_blocks", 1)
+    with pytest.raises(RuntimeError, match="injected"):
+        cache.save_block(key)
+    assert len(cache) == cache.bytes_used == 0 and key in m.hash_to_block_id
+    assert cache.save_block(key)
+    m.forget(key)
+    kvoff.debug_fail_next("copy_blocks", 1)
+    with pytest.raises(kvoff.KvoffError, match="injected"):
+        cache.restore_block(key)
+    assert key in cache and key not in m.hash_to_block_id
+    assert sorted(m.free_block_ids) == list(range(len(m.blocks))) and not m.used_block_ids
+    target = cache.restore_block(key)
+    cache.synchronize()
+    assert torch.equal(block_bytes(engine.pool, target), expected)
+
+
+def test_fp8_injected_failure_on_staged_save(cuda):
+    engine = FakeEngine(finite_pool(SHAPES[1], cuda))
+    key = engine.manager.publish(2)
+    cache = engine.create_cpu_prefix_cache(per_block(engine.pool), fp8=True)
+    kvoff.debug_fail_next("fp8_save_blocks_staged", 1)
+    with pytest.raises(RuntimeError, match="injected"):
+        cache.save_block(key)
+    assert len(cache) == 0 and cache._free_slots
+    assert cache.save_block(key)
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_measure_restore_s_per_block(cuda, fp8):
+    engine = FakeEngine(finite_pool(SHAPES[1], cuda))
+    cache = engine.create_cpu_prefix_cache(per_block(engine.pool), fp8=fp8, split_streams=True)
+    seconds = cache.measure_restore_s_per_block(repeats=4)
+    assert 0 < seconds < 1.0
+
+
+def test_prefetch_restore_orders_first_use(cuda):
+    engine = FakeEngine(arbitrary_pool(SHAPES[1], cuda))
+    m = engine.manager
+    key = m.publish(1)
+    expected = block_bytes(engine.pool, 1)
+    cache = engine.create_cpu_prefix_cache(per_block(engine.pool), automatic=True,
+                                           prefetch=True, split_streams=True)
+    assert cache.save_block(key)
+    cache.synchronize()
+    m.forget(key)
+    slow_copies(cache, ["_copy_entry"])
+    entry = cache._entries[key]
+    target = m.restore_cached_block(key, entry.token_ids,
+                                    lambda b: cache._copy_entry(entry, b, wait=False))
+    m.acquire_block(target)  # first reader: waits for the pending restore
+    got = engine.pool[:, :, target].contiguous().view(torch.uint8).cpu()
+    assert torch.equal(got, expected)
