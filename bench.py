@@ -1,23 +1,26 @@
 #!/usr/bin/env python
-"""KV-cache offload copy path benchmark (BASELINE config 2, one line of JSON).
+"""KV-cache offload copy path benchmark (one line of JSON).
 
-Workload (per GPU): a Qwen3-8B-shaped paged KV pool [2, 36, 320, 256, 8, 128]
-bf16 on the device (12.1 GB) filled with N(0,1) values and 1% x20 outlier
-channels per (K/V, layer, KV head), and a pinned NUMA-local host slab. One
-step saves 128 random blocks as FP8 while restoring 128 other saved blocks
-into 128 other GPU blocks, concurrently on a save stream and a restore stream.
+Default workload, BASELINE config 2, per GPU: a Qwen3-8B-shaped paged KV pool
+[2, 36, 320, 256, 8, 128] bf16 on the device (12.1 GB), filled with N(0,1)
+values and 1% x20 outlier channels per (K/V, layer, KV head), and a pinned
+NUMA-local host slab. One step saves 128 random blocks as FP8 while restoring
+128 other saved blocks into 128 other GPU blocks, concurrently on a save stream
+and a restore stream. `--workload config4` runs BASELINE config 4 instead: a
+Qwen3-32B pool sharded by KV head ([2, 64, 2048, 256, 8 / tp, 128] per rank),
+restoring 512 blocks (131,072 tokens) while saving 512 others.
 
-* value  - the same step with the slots in HBM (device-resident inputs): the
-           fused gather+quantize and dequantize+scatter kernels alone.
+* value  - the step with the slots in HBM (device-resident inputs): the fused
+           gather+quantize and dequantize+scatter kernels alone.
 * e2e    - the step through the C ABI with the slots in pinned host memory,
            PCIe transfers inside the timed region (save D2H, restore H2D).
-Both are GB/s of KV processed, counted as bf16 bytes (37.7 MB per block) for
-saves plus restores; tokens/s counts 256 tokens per block moved.
+Both are GB/s of KV processed, counted as bf16 bytes for saves plus restores;
+tokens/s counts block_size tokens per block moved.
 
 `--impl reference` times the reference algorithm on the host cores instead
 (the C oracle port of the reference's CPU-pool save / restore path).
-Multi-GPU (torchrun): every rank runs the same workload on its own GPU and
-slab (KV-head sharding needs no collective); time is the max over ranks.
+Multi-GPU (torchrun): every rank runs the workload on its own GPU and slab
+(KV-head sharding needs no collective); time is the max over ranks.
 """
 
 from __future__ import annotations
@@ -30,6 +33,7 @@ import subprocess
 import sys
 import tempfile
 import time
+from dataclasses import dataclass
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -37,22 +41,66 @@ for _p in (ROOT, ROOT / "kv-cache-offloading_b200"):
     if str(_p) not in sys.path:
         sys.path.insert(0, str(_p))
 
-LAYERS, NUM_BLOCKS, BLOCK_SIZE, HEADS, HEAD_DIM = 36, 320, 256, 8, 128
-ROWS = 2 * LAYERS * BLOCK_SIZE * HEADS
-BF16_BLOCK = ROWS * HEAD_DIM * 2          # 37,748,736 B
-FP8_PAYLOAD = ROWS * HEAD_DIM             # 18,874,368 B
-FP8_SCALE = ROWS * 2                      # 294,912 B
-FP8_BLOCK = FP8_PAYLOAD + FP8_SCALE       # 19,169,280 B
-KERNEL_BYTES = BF16_BLOCK + FP8_BLOCK     # HBM bytes one save or restore kernel moves per block
-# dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of the save
-# kernel on 8 config-2 blocks (profiles/fp8_save_kernel_config2.md), per block;
-# traffic scales with blocks because every block is read once and written once.
-SAVE_KERNEL_DRAM_BYTES_PER_BLOCK = (302_010_880 + 103_050_240) // 8
 SWEEP_BATCHES = (1, 8, 32, 128)
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "KV restore+save GB/s (FP8, bf16-equivalent bytes)"
-CONFIG_NAME = ("config2: Qwen3-8B-shaped paged KV [2,36,320,256,8,128] bf16; FP8 save of 128 "
-               "random blocks concurrent with FP8 restore of 128 others, split streams")
+# dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of the save
+# kernel on 8 config-2 blocks (profiles/fp8_save_kernel_config2.md), per byte of
+# bf16 block read; traffic scales with blocks because each is read and written once.
+SAVE_KERNEL_DRAM_BYTES_PER_BF16_BYTE = (302_010_880 + 103_050_240) / (8 * 37_748_736)
+
+
+@dataclass(frozen=True)
+class Workload:
+    name: str
+    layers: int
+    num_blocks: int
+    heads: int
+    batch: int
+    block_size: int = 256
+    head_dim: int = 128
+
+    @property
+    def rows(self) -> int:
+        return 2 * self.layers * self.block_size * self.heads
+
+    @property
+    def bf16_block(self) -> int:
+        return self.rows * self.head_dim * 2
+
+    @property
+    def fp8_payload(self) -> int:
+        return self.rows * self.head_dim
+
+    @property
+    def fp8_scale(self) -> int:
+        return self.rows * 2
+
+    @property
+    def fp8_block(self) -> int:
+        return self.fp8_payload + self.fp8_scale
+
+    @property
+    def kernel_bytes(self) -> int:
+        """HBM bytes one FP8 save (or restore) kernel moves per block."""
+        return self.bf16_block + self.fp8_block
+
+    def describe(self) -> str:
+        return (f"{self.name}: paged KV [2,{self.layers},{self.num_blocks},{self.block_size},"
+                f"{self.heads},{self.head_dim}] bf16 per GPU; FP8 save of {self.batch} random "
+                f"blocks concurrent with FP8 restore of {self.batch} others, split streams")
+
+
+def make_workload(args, world: int) -> Workload:
+    if args.workload == "config4":
+        tp = args.tp or world
+        if 8 % tp:
+            raise SystemExit("--tp must divide the 8 KV heads")
+        return Workload("config4 (Qwen3-32B, KV heads sharded tp=%d)" % tp, layers=64,
+                        num_blocks=args.pool_blocks or 2048, heads=8 // tp,
+                        batch=args.batch or 512)
+    return Workload("config2 (Qwen3-8B)", layers=36, num_blocks=args.pool_blocks or 320, heads=8,
+                    batch=args.batch or 128)
 
 
 def parse_args():
@@ -61,8 +109,10 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--batch", type=int, default=128, help="blocks saved and restored per step")
-    p.add_argument("--pool-blocks", type=int, default=NUM_BLOCKS,
+    p.add_argument("--workload", choices=("config2", "config4"), default="config2")
+    p.add_argument("--tp", type=int, default=0, help="config4 KV-head shards (default: --gpus)")
+    p.add_argument("--batch", type=int, default=0, help="blocks saved and restored per step")
+    p.add_argument("--pool-blocks", type=int, default=0,
                    help="GPU pool size in blocks (smaller pools are for profiler captures)")
     p.add_argument("--slab-gib", type=float, default=24.0, help="pinned host slab per GPU")
     p.add_argument("--no-sweep", action="store_true", help="skip the batch-size / mode sweep")
@@ -71,8 +121,6 @@ def parse_args():
     args = p.parse_args()
     if args.warmup < 3:
         p.error("--warmup must be >= 3")
-    if not 1 <= args.batch <= args.pool_blocks // 2:
-        p.error(f"--batch must be in [1, pool_blocks / 2]")
     return args
 
 
@@ -166,12 +214,11 @@ class ClockSampler:
 # --------------------------------------------------------------------------
 # reference arm: the reference's CPU-pool save/restore path, as the C oracle port
 
-
 _CPU_STATE: dict = {}
 
 
-def cpu_sample(seconds: float, threads: int | None = None) -> dict:
-    """Save + restore FP8 blocks of the config-2 shape on the host cores."""
+def cpu_sample(w: Workload, seconds: float, threads: int | None = None) -> dict:
+    """Save + restore FP8 blocks of the workload's shape on the host cores."""
     import numpy as np
 
     from oracle import oracle
@@ -179,20 +226,20 @@ def cpu_sample(seconds: float, threads: int | None = None) -> dict:
     if threads:
         oracle.set_threads(threads)
     cores = oracle.max_threads()
-    if "pool" not in _CPU_STATE:  # 4 blocks: 2 saved + 2 restored per iteration
+    if _CPU_STATE.get("workload") != w:  # 4 blocks: 2 saved + 2 restored per iteration
         rng = np.random.default_rng(0)
-        x = rng.standard_normal((2, LAYERS, 4, BLOCK_SIZE, HEADS, HEAD_DIM), dtype=np.float32)
+        x = rng.standard_normal((2, w.layers, 4, w.block_size, w.heads, w.head_dim),
+                                dtype=np.float32)
         u = x.view(np.uint32).astype(np.uint64)
         pool = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
-        _CPU_STATE["pool"] = pool
-        _CPU_STATE["slots"] = oracle.fp8_save_blocks(pool, [2, 3])
+        _CPU_STATE.update(workload=w, pool=pool,
+                          slots=oracle.fp8_save_blocks(pool, [2, 3], fast=True))
     pool = _CPU_STATE["pool"]
     payload, scale = _CPU_STATE["slots"]
 
     def step():
-        p, s = oracle.fp8_save_blocks(pool, [0, 1])
-        oracle.fp8_restore_blocks(pool, [2, 3], payload, scale)
-        return p, s
+        oracle.fp8_save_blocks(pool, [0, 1], fast=True)
+        oracle.fp8_restore_blocks(pool, [2, 3], payload, scale, fast=True)
 
     step()
     iters, start = 0, time.perf_counter()
@@ -202,34 +249,60 @@ def cpu_sample(seconds: float, threads: int | None = None) -> dict:
         elapsed = time.perf_counter() - start
         if elapsed >= seconds:
             break
-    gbps = iters * 4 * BF16_BLOCK / elapsed / 1e9
-    return {"value": gbps, "unit": "GB/s", "cores": cores, "kind": "port",
-            "sample": f"{iters} x (FP8 save of 2 + restore of 2 config-2 blocks), "
+    return {"value": iters * 4 * w.bf16_block / elapsed / 1e9, "unit": "GB/s", "cores": cores,
+            "kind": "port",
+            "sample": f"{iters} x (FP8 save of 2 + restore of 2 blocks of the workload shape), "
                       f"{elapsed:.1f} s on {cores} OpenMP threads",
-            "tokens_per_s": iters * 4 * BLOCK_SIZE / elapsed,
+            "tokens_per_s": iters * 4 * w.block_size / elapsed,
             "ms_per_block": 1000 * elapsed / (iters * 4)}
+
+
+def torch_ops_sample(w: Workload, seconds: float) -> dict:
+    """The reference's own CPU-pool path: its torch op chain on CPU tensors."""
+    import numpy as np
+    import torch
+
+    from kvoff.cpu_prefix_cache import fp8_dequantize, fp8_quantize
+
+    bits = _CPU_STATE["pool"]
+    pool = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16)
+    shape = (2, w.layers, w.block_size, w.heads, w.head_dim)
+    payload = torch.empty(shape, dtype=torch.float8_e4m3fn)
+    scale = torch.empty((*shape[:-1], 1), dtype=torch.bfloat16)
+    iters, start = 0, time.perf_counter()
+    while True:
+        fp8_quantize(pool[:, :, 0], payload, scale)
+        fp8_dequantize(payload, scale, pool[:, :, 2])
+        iters += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= seconds:
+            break
+    return {"GBps": iters * 2 * w.bf16_block / elapsed / 1e9, "threads": torch.get_num_threads(),
+            "what": "reference fp8_quantize + fp8_dequantize torch ops on host tensors"}
 
 
 def run_reference(args) -> None:
     rank, _, world = dist_env()
     if rank != 0:
         return  # rank 0 alone runs the host-core baseline
+    w = make_workload(args, world)
     per_step = max(0.5, min(5.0, 120.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
-        cpu_sample(per_step / 4)
-    samples = [cpu_sample(per_step) for _ in range(args.steps)]
+        cpu_sample(w, per_step / 4)
+    samples = [cpu_sample(w, per_step) for _ in range(args.steps)]
     value = statistics.mean(s["value"] for s in samples)
-    ms_per_step = statistics.mean(s["ms_per_block"] for s in samples) * 4
     emit({"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
           "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-          "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-          "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seed 0",
-          "config": {"workload": CONFIG_NAME, "batch_blocks": 2,
+          "ms_per_step": statistics.mean(s["ms_per_block"] for s in samples) * 4,
+          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+          "data": "synthetic N(0,1), seed 0",
+          "config": {"workload": w.describe(), "batch_blocks": 2,
                      "note": "host-core sample of the workload: each step saves 2 and "
-                             "restores 2 blocks of the config-2 shape"},
+                             "restores 2 blocks of the same shape"},
           "cpu_baseline": {"value": value, "unit": "GB/s", "cores": samples[0]["cores"],
                            "kind": "port", "sample": samples[0]["sample"]},
           "tokens_per_s": statistics.mean(s["tokens_per_s"] for s in samples),
+          "torch_ops_cpu": torch_ops_sample(w, per_step),
           "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
                   "d2h_bytes_per_step": 0}})
 
@@ -238,19 +311,22 @@ def run_reference(args) -> None:
 # our arm
 
 
-def fill_pool(pool, seed: int) -> None:
+def fill_pool(pool, heads: int, seed: int) -> None:
     """N(0,1) with 1% of (K/V, layer, KV head, channel) channels scaled x20."""
     import torch
 
     gen = torch.Generator(device=pool.device)
     gen.manual_seed(seed)
     two, layers = pool.shape[:2]
-    mask = torch.rand((two, layers, HEADS, HEAD_DIM), generator=gen, device=pool.device) < 0.01
+    mask = torch.rand((two, layers, heads, pool.shape[-1]), generator=gen,
+                      device=pool.device) < 0.01
     scale = torch.where(mask, 20.0, 1.0)
     for kv in range(two):
         for layer in range(layers):
-            chunk = torch.randn(pool[kv, layer].shape, generator=gen, device=pool.device)
-            pool[kv, layer].copy_(chunk.mul_(scale[kv, layer]))
+            for first in range(0, pool.shape[2], 256):  # bounded fp32 temporaries
+                part = pool[kv, layer, first:first + 256]
+                chunk = torch.randn(part.shape, generator=gen, device=pool.device)
+                part.copy_(chunk.mul_(scale[kv, layer]))
 
 
 class Timer:
@@ -300,6 +376,10 @@ def run_ours(args) -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device")
+    w = make_workload(args, world)
+    B = w.batch
+    if not 1 <= B <= w.num_blocks // 2:
+        raise SystemExit("the batch must be at most half the pool")
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
@@ -307,23 +387,25 @@ def run_ours(args) -> None:
 
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300),
                                              device_id=device)
-    B = args.batch
     main = torch.cuda.current_stream(device)
     save_stream = torch.cuda.Stream(device)
     restore_stream = torch.cuda.Stream(device)
     timer = Timer(torch, main, world)
+    sweep_batches = [b for b in SWEEP_BATCHES if b <= B] if not args.no_sweep else []
+    bf16_batch = max(sweep_batches, default=0)
 
-    pool = torch.empty((2, LAYERS, args.pool_blocks, BLOCK_SIZE, HEADS, HEAD_DIM),
+    pool = torch.empty((2, w.layers, w.num_blocks, w.block_size, w.heads, w.head_dim),
                        dtype=torch.bfloat16, device=device)
-    fill_pool(pool, seed=1000 + rank)
-    g = ops.geometry(pool)
+    fill_pool(pool, w.heads, seed=1000 + rank)
     rng = np.random.default_rng(rank)
-    perm = rng.permutation(args.pool_blocks)
+    perm = rng.permutation(w.num_blocks)
     save_ids = [int(i) for i in perm[:B]]
     restore_ids = [int(i) for i in perm[B:2 * B]]
 
-    # Host slab: FP8 slots for B saves + B restore sources, and BF16 slots for the sweep.
-    need = 2 * B * FP8_BLOCK + 2 * B * BF16_BLOCK
+    # Host slab: FP8 slots for B saves + B restore sources (payloads first,
+    # then scales, as in a CPU-tier slab chunk), then BF16 slots for the sweep.
+    fp8_bytes = 2 * B * w.fp8_block
+    need = fp8_bytes + 2 * bf16_batch * w.bf16_block
     local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
     budget = int(0.6 * mem_available_bytes() / max(1, local_world))
     slab_bytes = int(args.slab_gib * (1 << 30))
@@ -333,42 +415,48 @@ def run_ours(args) -> None:
     t0 = time.perf_counter()
     slab = PinnedSlab(slab_bytes, device=local_rank)
     pin_s = time.perf_counter() - t0
-    fp8_base, bf16_base = 0, 2 * B * FP8_BLOCK
 
-    def fp8_slot(i):  # (payload, scale) of FP8 slot i: payloads first, then scales
-        return (slab.view(fp8_base + i * FP8_PAYLOAD, (FP8_PAYLOAD,), torch.uint8),
-                slab.view(fp8_base + 2 * B * FP8_PAYLOAD + i * FP8_SCALE, (FP8_SCALE,),
-                          torch.uint8))
+    def fp8_slot(i):
+        return (slab.view(i * w.fp8_payload, (w.fp8_payload,), torch.uint8),
+                slab.view(2 * B * w.fp8_payload + i * w.fp8_scale, (w.fp8_scale,), torch.uint8))
 
     save_slots = [fp8_slot(i) for i in range(B)]
     restore_slots = [fp8_slot(B + i) for i in range(B)]
     host_ptr = lambda slots, k: [s[k].data_ptr() for s in slots]  # noqa: E731
     mapped_ptr = lambda slots, k: [slab.device_alias(s[k]) for s in slots]  # noqa: E731
-    bf16_slots = [slab.view(bf16_base + i * BF16_BLOCK, (BF16_BLOCK,), torch.uint8)
-                  for i in range(2 * B)]
+    bf16_slots = [slab.view(fp8_bytes + i * w.bf16_block, (w.bf16_block,), torch.uint8)
+                  for i in range(2 * bf16_batch)]
 
     staging_blocks = min(B, 16)
-    staging = {name: (torch.empty((staging_blocks, FP8_PAYLOAD), dtype=torch.uint8, device=device),
-                      torch.empty((staging_blocks, FP8_SCALE), dtype=torch.uint8, device=device))
+    staging = {name: (torch.empty((staging_blocks, w.fp8_payload), dtype=torch.uint8,
+                                  device=device),
+                      torch.empty((staging_blocks, w.fp8_scale), dtype=torch.uint8,
+                                  device=device))
                for name in ("save", "restore")}
-    bf16_staging = {name: torch.empty((staging_blocks, BF16_BLOCK), dtype=torch.uint8, device=device)
-                    for name in ("save", "restore")}
+    bf16_staging = {name: torch.empty((staging_blocks, w.bf16_block), dtype=torch.uint8,
+                                      device=device) for name in ("save", "restore")} \
+        if bf16_batch else {}
 
     # Restore sources hold real FP8 blocks (saved once, untimed).
-    ops.save_fp8_staged(pool, restore_ids, host_ptr(restore_slots, 0), host_ptr(restore_slots, 1),
-                        *staging["save"], stream=main)
+    ops.save_fp8_staged(pool, restore_ids, host_ptr(restore_slots, 0),
+                        host_ptr(restore_slots, 1), *staging["save"], stream=main)
     torch.cuda.synchronize()
 
     # ---- device-resident step (value): slots in HBM -------------------------
-    dev_save = (torch.empty((B, FP8_PAYLOAD), dtype=torch.uint8, device=device),
-                torch.empty((B, FP8_SCALE), dtype=torch.uint8, device=device))
-    dev_src = (torch.empty((B, FP8_PAYLOAD), dtype=torch.uint8, device=device),
-               torch.empty((B, FP8_SCALE), dtype=torch.uint8, device=device))
-    for i, (p, s) in enumerate(restore_slots):
-        dev_src[0][i].copy_(p)
-        dev_src[1][i].copy_(s)
-    dsp, dss = [t.data_ptr() for t in dev_save[0]], [t.data_ptr() for t in dev_save[1]]
-    drp, drs = [t.data_ptr() for t in dev_src[0]], [t.data_ptr() for t in dev_src[1]]
+    # A ring of at most 128 device slots per direction (reused round robin when
+    # the batch is larger: same bytes moved, far more than L2 holds).
+    ring = min(B, 128)
+    dev_save = (torch.empty((ring, w.fp8_payload), dtype=torch.uint8, device=device),
+                torch.empty((ring, w.fp8_scale), dtype=torch.uint8, device=device))
+    dev_src = (torch.empty((ring, w.fp8_payload), dtype=torch.uint8, device=device),
+               torch.empty((ring, w.fp8_scale), dtype=torch.uint8, device=device))
+    for i in range(ring):
+        dev_src[0][i].copy_(restore_slots[i][0])
+        dev_src[1][i].copy_(restore_slots[i][1])
+    dsp = [dev_save[0][i % ring].data_ptr() for i in range(B)]
+    dss = [dev_save[1][i % ring].data_ptr() for i in range(B)]
+    drp = [dev_src[0][i % ring].data_ptr() for i in range(B)]
+    drs = [dev_src[1][i % ring].data_ptr() for i in range(B)]
 
     def concurrent(save_fn, restore_fn):
         def step():
@@ -389,9 +477,8 @@ def run_ours(args) -> None:
     gpu_name = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
     with ClockSampler(gpu_name) as clocks_dev:
         ms = timer.run(device_step, args.steps, args.warmup)
-    ms = max_over_ranks(torch, ms, device)
-    dev_ms_per_step = ms / args.steps
-    value = world * 2 * B * BF16_BLOCK / (dev_ms_per_step / 1e3) / 1e9
+    dev_ms_per_step = max_over_ranks(torch, ms, device) / args.steps
+    value = world * 2 * B * w.bf16_block / (dev_ms_per_step / 1e3) / 1e9
 
     # ---- roofline: each kernel alone, timed on its own stream ----------------
     def kernel_alone(fn, stream):
@@ -406,21 +493,23 @@ def run_ours(args) -> None:
                                                       stream=restore_stream), restore_stream)
     peaks = measured_peaks()
     hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
-    peak_source = "MEASURED_PEAKS.json hbm_gbs (burst copy)" if "hbm_gbs" in peaks else \
-        "fallback 6650 GB/s"
+    peak_source = ("MEASURED_PEAKS.json hbm_gbs (burst copy)" if "hbm_gbs" in peaks
+                   else "fallback 6650 GB/s")
     save_launch_ms = save_ms / launches_per_call
     blocks_per_launch = B / launches_per_call
-    achieved = blocks_per_launch * KERNEL_BYTES / (save_launch_ms / 1e3) / 1e9
-    restore_achieved = blocks_per_launch * KERNEL_BYTES / (restore_ms / launches_per_call / 1e3) / 1e9
-    traffic = SAVE_KERNEL_DRAM_BYTES_PER_BLOCK * blocks_per_launch
+    achieved = blocks_per_launch * w.kernel_bytes / (save_launch_ms / 1e3) / 1e9
+    restore_launch_ms = restore_ms / launches_per_call
+    restore_achieved = blocks_per_launch * w.kernel_bytes / (restore_launch_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                "frac": achieved / hbm_peak, "traffic": traffic,
-                "kernel": "fp8_save_kernel (gather + quantize, 128 blocks per launch)",
-                "peak_source": peak_source,
-                "algorithmic_bytes_per_block": KERNEL_BYTES,
+                "frac": achieved / hbm_peak,
+                "traffic": SAVE_KERNEL_DRAM_BYTES_PER_BF16_BYTE * w.bf16_block * blocks_per_launch,
+                "kernel": f"fp8_save_kernel (gather + quantize, {int(blocks_per_launch)} blocks "
+                          "per launch)",
+                "peak_source": peak_source, "algorithmic_bytes_per_block": w.kernel_bytes,
                 "launch_ms": save_launch_ms,
-                "restore_kernel": {"achieved": restore_achieved, "frac": restore_achieved / hbm_peak,
-                                   "launch_ms": restore_ms / launches_per_call}}
+                "restore_kernel": {"achieved": restore_achieved,
+                                   "frac": restore_achieved / hbm_peak,
+                                   "launch_ms": restore_launch_ms}}
 
     # ---- end to end through the C ABI with pinned host slots -----------------
     def e2e_fns(batch, save_mode, restore_mode):
@@ -431,8 +520,8 @@ def run_ours(args) -> None:
             save = lambda: ops.save_fp8(pool, sids, sp, sc, stream=save_stream)  # noqa: E731
         else:
             sp, sc = host_ptr(ss, 0), host_ptr(ss, 1)
-            save = lambda: ops.save_fp8_staged(pool, sids, sp, sc, *staging["save"],  # noqa: E731
-                                               stream=save_stream)
+            save = lambda: ops.save_fp8_staged(pool, sids, sp, sc,  # noqa: E731
+                                               *staging["save"], stream=save_stream)
         if restore_mode == "mapped":
             rp, rc = mapped_ptr(rs, 0), mapped_ptr(rs, 1)
             restore = lambda: ops.restore_fp8(pool, rids, rp, rc,  # noqa: E731
@@ -445,7 +534,7 @@ def run_ours(args) -> None:
 
     def bf16_fns(batch, method):
         sids, rids = save_ids[:batch], restore_ids[:batch]
-        ss, rs = bf16_slots[:batch], bf16_slots[B:B + batch]
+        ss, rs = bf16_slots[:batch], bf16_slots[bf16_batch:bf16_batch + batch]
         if method == "tma":
             st_s, st_r = bf16_staging["save"], bf16_staging["restore"]
 
@@ -454,16 +543,14 @@ def run_ours(args) -> None:
                     n = min(staging_blocks, batch - k)
                     ops.copy_blocks(pool, sids[k:k + n], [x.data_ptr() for x in st_s[:n]],
                                     method=ops.COPY_TMA, stream=save_stream)
-                    for j in range(n):
-                        ops.memcpy(ss[k + j].data_ptr(), st_s[j].data_ptr(), BF16_BLOCK,
-                                   device=device, stream=save_stream)
+                    ops.memcpy(ss[k].data_ptr(), st_s.data_ptr(), n * w.bf16_block,
+                               device=device, stream=save_stream)
 
             def restore():
                 for k in range(0, batch, staging_blocks):
                     n = min(staging_blocks, batch - k)
-                    for j in range(n):
-                        ops.memcpy(st_r[j].data_ptr(), rs[k + j].data_ptr(), BF16_BLOCK,
-                                   device=device, stream=restore_stream)
+                    ops.memcpy(st_r.data_ptr(), rs[k].data_ptr(), n * w.bf16_block,
+                               device=device, stream=restore_stream)
                     ops.copy_blocks(pool, rids[k:k + n], [x.data_ptr() for x in st_r[:n]],
                                     restore=True, method=ops.COPY_TMA, stream=restore_stream)
             return save, restore
@@ -471,95 +558,87 @@ def run_ours(args) -> None:
         sp = [slab.device_alias(x) if method == "sm" else x.data_ptr() for x in ss]
         rp = [slab.device_alias(x) if method == "sm" else x.data_ptr() for x in rs]
         save = lambda: ops.copy_blocks(pool, sids, sp, method=code, stream=save_stream)  # noqa
-        restore = lambda: ops.copy_blocks(pool, rids, rp, restore=True, method=code,  # noqa
-                                          stream=restore_stream)
+        restore = lambda: ops.copy_blocks(pool, rids, rp, restore=True,  # noqa: E731
+                                          method=code, stream=restore_stream)
         return save, restore
 
     def rate(step, batch, directions, steps, warmup):
         ms = timer.run(step, steps, warmup) / steps
-        return directions * batch * BF16_BLOCK / (ms / 1e3) / 1e9, ms
+        return directions * batch * w.bf16_block / (ms / 1e3) / 1e9
 
     sweep = {}
-    if not args.no_sweep:
-        few = dict(steps=4, warmup=3)
-        for batch in SWEEP_BATCHES:
-            if batch > B:
-                continue
-            row = {}
-            for mode in ("staged", "mapped"):
-                save, restore = e2e_fns(batch, mode, mode)
-                row[f"fp8_{mode}"] = {
-                    "save": rate(concurrent(save, lambda: None), batch, 1, **few)[0],
-                    "restore": rate(concurrent(lambda: None, restore), batch, 1, **few)[0],
-                    "duplex": rate(concurrent(save, restore), batch, 2, **few)[0]}
-            for save_m, restore_m in (("mapped", "staged"), ("staged", "mapped")):
-                save, restore = e2e_fns(batch, save_m, restore_m)
-                row[f"fp8_save_{save_m}_restore_{restore_m}"] = {
-                    "duplex": rate(concurrent(save, restore), batch, 2, **few)[0]}
-            for method in ("engine", "tma", "sm"):
-                save, restore = bf16_fns(batch, method)
-                row[f"bf16_{method}"] = {
-                    "save": rate(concurrent(save, lambda: None), batch, 1, **few)[0],
-                    "restore": rate(concurrent(lambda: None, restore), batch, 1, **few)[0],
-                    "duplex": rate(concurrent(save, restore), batch, 2, **few)[0]}
-            sweep[str(batch)] = row
-        best = sweep.get(str(B), {})
+    few = dict(steps=4, warmup=3)
+    for batch in sweep_batches:
+        row = {}
+        for mode in ("staged", "mapped"):
+            save, restore = e2e_fns(batch, mode, mode)
+            row[f"fp8_{mode}"] = {
+                "save": rate(concurrent(save, lambda: None), batch, 1, **few),
+                "restore": rate(concurrent(lambda: None, restore), batch, 1, **few),
+                "duplex": rate(concurrent(save, restore), batch, 2, **few)}
+        for save_m, restore_m in (("mapped", "staged"), ("staged", "mapped")):
+            save, restore = e2e_fns(batch, save_m, restore_m)
+            row[f"fp8_save_{save_m}_restore_{restore_m}"] = {
+                "duplex": rate(concurrent(save, restore), batch, 2, **few)}
+        for method in ("engine", "tma", "sm"):
+            save, restore = bf16_fns(batch, method)
+            row[f"bf16_{method}"] = {
+                "save": rate(concurrent(save, lambda: None), batch, 1, **few),
+                "restore": rate(concurrent(lambda: None, restore), batch, 1, **few),
+                "duplex": rate(concurrent(save, restore), batch, 2, **few)}
+        sweep[str(batch)] = row
+    best = sweep.get(str(bf16_batch), {})
 
-        def duplex(save_m, restore_m):
-            key = f"fp8_{save_m}" if save_m == restore_m else \
-                f"fp8_save_{save_m}_restore_{restore_m}"
-            return best.get(key, {}).get("duplex", 0.0)
-        combos = [(a, b) for a in ("staged", "mapped") for b in ("staged", "mapped")]
-        save_mode, restore_mode = max(combos, key=lambda c: duplex(*c)) if best else \
-            ("staged", "staged")
-    else:
-        save_mode = restore_mode = "staged"
+    def duplex(save_m, restore_m):
+        key = (f"fp8_{save_m}" if save_m == restore_m
+               else f"fp8_save_{save_m}_restore_{restore_m}")
+        return best.get(key, {}).get("duplex", 0.0)
+
+    combos = [(a, b) for a in ("staged", "mapped") for b in ("staged", "mapped")]
+    save_mode, restore_mode = max(combos, key=lambda c: duplex(*c)) if best else \
+        ("staged", "staged")
 
     save, restore = e2e_fns(B, save_mode, restore_mode)
-    e2e_step = concurrent(save, restore)
     with ClockSampler(gpu_name) as clocks_e2e:
-        ms = timer.run(e2e_step, args.steps, args.warmup)
-    ms = max_over_ranks(torch, ms, device)
-    e2e_ms = ms / args.steps
-    e2e_value = world * 2 * B * BF16_BLOCK / (e2e_ms / 1e3) / 1e9
-    launches = 0
-    launches += launches_per_call if save_mode == "mapped" else -(-B // staging_blocks)
-    launches += launches_per_call if restore_mode == "mapped" else -(-B // staging_blocks)
+        ms = timer.run(concurrent(save, restore), args.steps, args.warmup)
+    e2e_ms = max_over_ranks(torch, ms, device) / args.steps
+    e2e_value = world * 2 * B * w.bf16_block / (e2e_ms / 1e3) / 1e9
+    groups = -(-B // max(1, staging_blocks // 2))
+    launches = (launches_per_call if save_mode == "mapped" else groups) + \
+        (launches_per_call if restore_mode == "mapped" else groups)
 
-    # ---- PCIe ceiling: contiguous pinned memcpy per direction and duplex -------
-    n_bytes = min(B, 64) * FP8_BLOCK
+    # ---- PCIe ceiling: pinned memcpy per direction and duplex -------------------
+    blocks = min(B, 64, max(1, int(2.5e9 // w.fp8_block)))
+    n_bytes = blocks * w.fp8_block
     dev_buf = torch.empty(2 * n_bytes, dtype=torch.uint8, device=device)
-    h_d2h = slab.bytes[fp8_base:fp8_base + n_bytes]
-    h_h2d = slab.bytes[fp8_base + n_bytes:fp8_base + 2 * n_bytes]
-    d2h = lambda: h_d2h.copy_(dev_buf[:n_bytes], non_blocking=True)  # noqa: E731
-    h2d = lambda: dev_buf[n_bytes:].copy_(h_h2d, non_blocking=True)  # noqa: E731
+    h_d2h, h_h2d = slab.bytes[:n_bytes], slab.bytes[n_bytes:2 * n_bytes]
+    cp = lambda d, s_: d.copy_(s_, non_blocking=True)  # noqa: E731
+
+    def chunked(dst, src):
+        return lambda: [cp(dst[k * w.fp8_block:(k + 1) * w.fp8_block],
+                           src[k * w.fp8_block:(k + 1) * w.fp8_block]) for k in range(blocks)]
 
     def memcpy_rate(step, directions):
         ms = timer.run(step, 5, 3) / 5
         return directions * n_bytes / (ms / 1e3) / 1e9
 
-    per_block = n_bytes // FP8_BLOCK
-
-    def chunked(copy, dst, src):
-        return lambda: [copy(dst[k * FP8_BLOCK:(k + 1) * FP8_BLOCK],
-                             src[k * FP8_BLOCK:(k + 1) * FP8_BLOCK]) for k in range(per_block)]
-
-    cp = lambda d, s_: d.copy_(s_, non_blocking=True)  # noqa: E731
+    d2h = lambda: cp(h_d2h, dev_buf[:n_bytes])  # noqa: E731
+    h2d = lambda: cp(dev_buf[n_bytes:], h_h2d)  # noqa: E731
     ceiling = {"d2h": memcpy_rate(concurrent(d2h, lambda: None), 1),
                "h2d": memcpy_rate(concurrent(lambda: None, h2d), 1),
                "duplex_total": memcpy_rate(concurrent(d2h, h2d), 2),
                "duplex_total_block_copies": memcpy_rate(
-                   concurrent(chunked(cp, h_d2h, dev_buf[:n_bytes]),
-                              chunked(cp, dev_buf[n_bytes:], h_h2d)), 2),
+                   concurrent(chunked(h_d2h, dev_buf[:n_bytes]),
+                              chunked(dev_buf[n_bytes:], h_h2d)), 2),
                "bytes_per_copy": n_bytes}
-    pcie_per_dir = B * FP8_BLOCK / (e2e_ms / 1e3) / 1e9
+    del dev_buf
+    pcie_per_dir = B * w.fp8_block / (e2e_ms / 1e3) / 1e9
 
     # ---- the reference's device path (torch ops) for context ------------------
-    ref_gpu = None
     try:
         from kvoff.cpu_prefix_cache import fp8_dequantize, fp8_quantize
 
-        shape = (2, LAYERS, BLOCK_SIZE, HEADS, HEAD_DIM)
+        shape = (2, w.layers, w.block_size, w.heads, w.head_dim)
         stage_p = torch.empty(shape, dtype=torch.float8_e4m3fn, device=device)
         stage_s = torch.empty((*shape[:-1], 1), dtype=torch.bfloat16, device=device)
         few_ids = save_ids[:8]
@@ -570,29 +649,31 @@ def run_ours(args) -> None:
                 fp8_dequantize(stage_p, stage_s, pool[:, :, restore_ids[0]])
         ms = Timer(torch, main, 1).run(aten_step, 3, 3) / 3
         ref_gpu = {"what": "reference fp8_quantize + fp8_dequantize as torch ops on this GPU",
-                   "GBps": 2 * len(few_ids) * BF16_BLOCK / (ms / 1e3) / 1e9}
+                   "GBps": 2 * len(few_ids) * w.bf16_block / (ms / 1e3) / 1e9}
     except Exception as exc:  # context only; never fails the bench
         ref_gpu = {"error": str(exc)[:200]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_sample(args.cpu_seconds)
+        cpu = cpu_sample(w, args.cpu_seconds)
+        cpu["torch_ops_cpu"] = torch_ops_sample(w, min(5.0, args.cpu_seconds))
 
-    clocks = clocks_e2e.summary() or clocks_dev.summary()
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: N(0,1) bf16 with 1% x20 outlier channels per (K/V, layer, KV head)",
-        "config": {"workload": CONFIG_NAME, "batch_blocks": B, "pool_blocks": args.pool_blocks,
-                   "pool_bytes": pool.numel() * 2,
-                   "slab_bytes": slab_bytes, "slab_pin_s": pin_s, "numa_node": slab.numa_node,
-                   "l2": "inputs larger than L2 (4.8 GB of KV per step)",
-                   "parallelism": f"dp{world} (independent per-GPU pools and slabs, no collective)"},
-        "tokens_per_s": world * 2 * B * BLOCK_SIZE / (dev_ms_per_step / 1e3),
-        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": B * FP8_BLOCK,
-                "d2h_bytes_per_step": B * FP8_BLOCK, "ms_per_step": e2e_ms,
-                "tokens_per_s": world * 2 * B * BLOCK_SIZE / (e2e_ms / 1e3),
+        "config": {"workload": w.describe(), "batch_blocks": B, "pool_blocks": w.num_blocks,
+                   "pool_bytes": pool.numel() * 2, "slab_bytes": slab_bytes,
+                   "slab_pin_s": pin_s, "numa_node": slab.numa_node,
+                   "l2": f"inputs larger than L2 ({2 * B * w.bf16_block / 1e9:.1f} GB of KV "
+                         "per step)",
+                   "parallelism": f"dp{world} (independent per-GPU pools and slabs, no "
+                                  "collective)"},
+        "tokens_per_s": world * 2 * B * w.block_size / (dev_ms_per_step / 1e3),
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": B * w.fp8_block,
+                "d2h_bytes_per_step": B * w.fp8_block, "ms_per_step": e2e_ms,
+                "tokens_per_s": world * 2 * B * w.block_size / (e2e_ms / 1e3),
                 "save_mode": save_mode, "restore_mode": restore_mode,
                 "pcie_GBps_per_direction": pcie_per_dir,
                 "pcie_frac_of_memcpy_d2h": pcie_per_dir / ceiling["d2h"],
@@ -600,7 +681,7 @@ def run_ours(args) -> None:
                 "pcie_frac_of_memcpy_duplex": 2 * pcie_per_dir / ceiling["duplex_total"]},
         "roofline": roofline,
         "cpu_baseline": cpu,
-        "clocks": clocks,
+        "clocks": clocks_e2e.summary() or clocks_dev.summary(),
         "gpu_launches": launches * args.steps,
         "pcie_memcpy_ceiling_GBps": ceiling,
         "sweep_GBps": sweep,

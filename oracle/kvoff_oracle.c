@@ -307,3 +307,100 @@ ORACLE_API int32_t kvo_scale_multiply_mismatches(void) {
   }
   return bad;
 }
+
+/*
+ * Fast single-pass port of the same path, for the timed CPU baseline (the
+ * bench's reference arm). The reference runs these steps as separate torch
+ * ops with fp32 temporaries; this port fuses them per row and rounds with
+ * integer bit operations, so it is a faster (conservative) CPU baseline. Its
+ * results equal the checker above bit for bit (tests/test_oracle_port.py);
+ * rows holding Inf or NaN go through the checker's row routine.
+ */
+static float g_e4m3_table[256];
+static int g_e4m3_table_ready = 0;
+
+static void init_e4m3_table(void) {
+  if (g_e4m3_table_ready) return;
+  for (int v = 0; v < 256; ++v) g_e4m3_table[v] = e4m3_value((uint8_t)v);
+  g_e4m3_table_ready = 1;
+}
+
+static inline uint32_t rne16_bits(float f) { /* finite f: bf16 bits, RNE */
+  const uint32_t u = f32_to_bits(f);
+  return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+}
+
+/* e4m3 byte of a finite q with |q| <= 448, round to nearest even. */
+static inline uint8_t e4m3_bits_clamped(float q) {
+  const uint32_t u = f32_to_bits(q);
+  const uint32_t a = u & 0x7FFFFFFFu;
+  uint32_t mag;
+  if (a < 0x3C800000u) /* below 2^-6: grid of 2^-9 (subnormals) */
+    mag = (uint32_t)rintf(bits_to_f32(a) * 512.0f);
+  else /* keep 3 mantissa bits, rebias the exponent from 127 to 7 */
+    mag = ((a + 0x7FFFFu + ((a >> 20) & 1u)) >> 20) - (120u << 3);
+  return (uint8_t)(((u >> 24) & 0x80u) | mag);
+}
+
+static void quantize_row_fast(const uint16_t* x, int64_t d, uint8_t* out, uint16_t* scale) {
+  uint32_t m = 0;
+  for (int64_t j = 0; j < d; ++j) {
+    const uint32_t a = x[j] & 0x7FFFu;
+    m = a > m ? a : m;
+  }
+  if (m >= 0x7F80u) { /* an Inf or NaN in the row */
+    quantize_row(x, d, out, scale);
+    return;
+  }
+  float s32 = bf16_value((uint16_t)m) / 448.0f;
+  if (s32 < 1e-30f) s32 = 1e-30f;
+  const uint16_t sb = (uint16_t)rne16_bits(s32);
+  const float s = bf16_value(sb);
+  *scale = sb;
+  for (int64_t j = 0; j < d; ++j) {
+    float q = bf16_value(x[j]) / s;
+    q = q < -448.0f ? -448.0f : (q > 448.0f ? 448.0f : q);
+    out[j] = e4m3_bits_clamped(q);
+  }
+}
+
+static void dequantize_row_fast(const uint8_t* p, uint16_t scale, int64_t d, uint16_t* out) {
+  const float s = bf16_value(scale);
+  for (int64_t j = 0; j < d; ++j) {
+    const float v = g_e4m3_table[p[j]] * s;
+    const uint32_t u = f32_to_bits(v);
+    out[j] = (u & 0x7FFFFFFFu) > 0x7F800000u ? 0x7FFF : (uint16_t)rne16_bits(v);
+  }
+}
+
+ORACLE_API void kvo_fp8_save_blocks_fast(const uint16_t* pool, int64_t num_chunks,
+                                         int64_t chunk_stride, int64_t block_stride,
+                                         int64_t rows_per_chunk, int64_t d, const int64_t* ids,
+                                         int64_t count, uint8_t* payload, uint16_t* scale) {
+  const int64_t rows = num_chunks * rows_per_chunk;
+  const int64_t total = count * rows;
+#pragma omp parallel for schedule(static)
+  for (int64_t q = 0; q < total; ++q) {
+    const int64_t i = q / rows, sr = q % rows;
+    const int64_t c = sr / rows_per_chunk, r = sr % rows_per_chunk;
+    quantize_row_fast(pool + c * chunk_stride + ids[i] * block_stride + r * d, d,
+                      payload + (i * rows + sr) * d, scale + i * rows + sr);
+  }
+}
+
+ORACLE_API void kvo_fp8_restore_blocks_fast(uint16_t* pool, int64_t num_chunks,
+                                            int64_t chunk_stride, int64_t block_stride,
+                                            int64_t rows_per_chunk, int64_t d, const int64_t* ids,
+                                            int64_t count, const uint8_t* payload,
+                                            const uint16_t* scale) {
+  init_e4m3_table();
+  const int64_t rows = num_chunks * rows_per_chunk;
+  const int64_t total = count * rows;
+#pragma omp parallel for schedule(static)
+  for (int64_t q = 0; q < total; ++q) {
+    const int64_t i = q / rows, sr = q % rows;
+    const int64_t c = sr / rows_per_chunk, r = sr % rows_per_chunk;
+    dequantize_row_fast(payload + (i * rows + sr) * d, scale[i * rows + sr], d,
+                        pool + c * chunk_stride + ids[i] * block_stride + r * d);
+  }
+}

@@ -41,6 +41,8 @@ def lib() -> ctypes.CDLL:
         so.kvo_fp8_dequantize_rows.argtypes = [_P, _P, _I, _I, _P, _I]
         so.kvo_fp8_save_blocks.argtypes = [_P, _I, _I, _I, _I, _I, _P, _I, _P, _P]
         so.kvo_fp8_restore_blocks.argtypes = [_P, _I, _I, _I, _I, _I, _P, _I, _P, _P]
+        so.kvo_fp8_save_blocks_fast.argtypes = [_P, _I, _I, _I, _I, _I, _P, _I, _P, _P]
+        so.kvo_fp8_restore_blocks_fast.argtypes = [_P, _I, _I, _I, _I, _I, _P, _I, _P, _P]
         so.kvo_copy_blocks.argtypes = [_P, _I, _I, _I, _I, _P, _I, _P, ctypes.c_int]
         so.kvo_store_kvcache.argtypes = [_P, _I, _P, _I, _P, _P, _I, _P, _I, _I]
         _lib = so
@@ -111,29 +113,34 @@ def _geometry(pool: np.ndarray) -> tuple[int, int, int, int, int]:
     return 2 * layers, nb * bs * h * d, bs * h * d, bs * h, d
 
 
-def fp8_save_blocks(pool: np.ndarray, ids) -> tuple[np.ndarray, np.ndarray]:
-    """Quantize pool[:, :, id] for each id -> payload [n, 2, L, BS, H, D], scale [n, ..., 1]."""
+def fp8_save_blocks(pool: np.ndarray, ids, fast: bool = False) -> tuple[np.ndarray, np.ndarray]:
+    """Quantize pool[:, :, id] for each id -> payload [n, 2, L, BS, H, D], scale [n, ..., 1].
+
+    fast=True runs the single-pass port (same bits) used as the timed CPU baseline.
+    """
     pool = np.asarray(pool)
     chunks, cs, bst, rpc, d = _geometry(pool)
     ids = np.ascontiguousarray(ids, dtype=np.int64)
     _, layers, _, bs, h, _ = pool.shape
     payload = np.empty((len(ids), 2, layers, bs, h, d), dtype=np.uint8)
     scale = np.empty((len(ids), 2, layers, bs, h, 1), dtype=np.uint16)
-    lib().kvo_fp8_save_blocks(_ptr(pool.view(np.uint16)), chunks, cs, bst, rpc, d, _ptr(ids),
-                              len(ids), _ptr(payload), _ptr(scale))
+    fn = lib().kvo_fp8_save_blocks_fast if fast else lib().kvo_fp8_save_blocks
+    fn(_ptr(pool.view(np.uint16)), chunks, cs, bst, rpc, d, _ptr(ids), len(ids), _ptr(payload),
+       _ptr(scale))
     return payload, scale
 
 
-def fp8_restore_blocks(pool: np.ndarray, ids, payload: np.ndarray, scale: np.ndarray) -> None:
-    """Dequantize slot i into pool[:, :, ids[i]] in place."""
+def fp8_restore_blocks(pool: np.ndarray, ids, payload: np.ndarray, scale: np.ndarray,
+                       fast: bool = False) -> None:
+    """Dequantize slot i into pool[:, :, ids[i]] in place (fast=True: the timed port)."""
     chunks, cs, bst, rpc, d = _geometry(pool)
     ids = np.ascontiguousarray(ids, dtype=np.int64)
     p = np.ascontiguousarray(payload, dtype=np.uint8)
     s = np.ascontiguousarray(scale, dtype=np.uint16)
     if p.shape[0] != len(ids) or s.shape[0] != len(ids):
         raise ValueError("one payload and scale slot per block id")
-    lib().kvo_fp8_restore_blocks(_ptr(pool.view(np.uint16)), chunks, cs, bst, rpc, d, _ptr(ids),
-                                 len(ids), _ptr(p), _ptr(s))
+    fn = lib().kvo_fp8_restore_blocks_fast if fast else lib().kvo_fp8_restore_blocks
+    fn(_ptr(pool.view(np.uint16)), chunks, cs, bst, rpc, d, _ptr(ids), len(ids), _ptr(p), _ptr(s))
 
 
 def copy_blocks(pool: np.ndarray, ids, slots: np.ndarray | None = None, restore: bool = False):
