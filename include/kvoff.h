@@ -180,6 +180,22 @@ KVOFF_API int kvoff_copy_blocks(void* pool, int64_t num_chunks, int64_t chunk_st
                                 int32_t max_ctas, void* stream);
 
 /*
+ * Token-range copy for KV handoff: the first num_tokens tokens of a sequence,
+ * stored in blocks block_ids[0 .. ceil(num_tokens / block_size)) of the pool,
+ * to or from a dense [2L, num_tokens, H, D] buffer (direction KVOFF_SAVE:
+ * pool -> dense, KVOFF_RESTORE: dense -> pool). token_bytes = H * D * elem;
+ * strides in bytes. One strided DMA per block (the last one partial); dense may
+ * be pinned host or device memory. Replaces the index_select + .contiguous() +
+ * .cpu() gather of export_kv (nanovllm/engine/kv_handoff.py:46-55) and the
+ * per-block scatter of import_kv (:112-118).
+ */
+KVOFF_API int kvoff_copy_tokens(void* pool, int64_t num_chunks, int64_t chunk_stride_bytes,
+                                int64_t block_stride_bytes, int64_t num_blocks,
+                                int64_t block_size, int64_t token_bytes,
+                                const int64_t* block_ids, int64_t num_tokens, void* dense,
+                                int32_t direction, void* stream);
+
+/*
  * Slot-mapping scatter of fresh K/V rows into the paged cache:
  *     for i < num_tokens with slot = slot_mapping[i] != -1:
  *         k_cache[slot * row_bytes ...] = key[i * key_stride_bytes ...] (row_bytes)

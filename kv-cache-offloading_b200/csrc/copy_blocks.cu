@@ -330,6 +330,42 @@ int kvoff_copy_blocks(void* pool, int64_t num_chunks, int64_t chunk_stride_bytes
   return ok();
 }
 
+int kvoff_copy_tokens(void* pool, int64_t num_chunks, int64_t chunk_stride_bytes,
+                      int64_t block_stride_bytes, int64_t num_blocks, int64_t block_size,
+                      int64_t token_bytes, const int64_t* block_ids, int64_t num_tokens,
+                      void* dense, int32_t direction, void* stream) {
+  if (injected("copy_tokens")) return KVOFF_EINJECTED;
+  if (num_tokens < 0 || num_chunks <= 0 || block_size <= 0 || token_bytes <= 0 ||
+      num_blocks <= 0 || chunk_stride_bytes < block_size * token_bytes || block_stride_bytes < 0)
+    return fail(KVOFF_EINVAL, "kvoff_copy_tokens: bad geometry");
+  if (direction != KVOFF_SAVE && direction != KVOFF_RESTORE)
+    return fail(KVOFF_EINVAL, "kvoff_copy_tokens: bad direction %d", direction);
+  if (num_tokens == 0) return ok();
+  if (pool == nullptr || dense == nullptr || block_ids == nullptr)
+    return fail(KVOFF_EINVAL, "kvoff_copy_tokens: null pointer");
+  const int64_t blocks = (num_tokens + block_size - 1) / block_size;
+  for (int64_t i = 0; i < blocks; ++i)
+    if (block_ids[i] < 0 || block_ids[i] >= num_blocks)
+      return fail(KVOFF_EINVAL, "kvoff_copy_tokens: block id %lld out of range [0, %lld)",
+                  (long long)block_ids[i], (long long)num_blocks);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t dense_pitch = num_tokens * token_bytes;  // one (K/V, layer) row of the dense copy
+  for (int64_t i = 0; i < blocks; ++i) {
+    const int64_t first = i * block_size;
+    const int64_t n = (num_tokens - first) < block_size ? (num_tokens - first) : block_size;
+    uint8_t* blk = static_cast<uint8_t*>(pool) + block_ids[i] * block_stride_bytes;
+    uint8_t* dn = static_cast<uint8_t*>(dense) + first * token_bytes;
+    const cudaError_t e =
+        direction == KVOFF_SAVE
+            ? cudaMemcpy2DAsync(dn, dense_pitch, blk, chunk_stride_bytes, n * token_bytes,
+                                num_chunks, cudaMemcpyDefault, s)
+            : cudaMemcpy2DAsync(blk, chunk_stride_bytes, dn, dense_pitch, n * token_bytes,
+                                num_chunks, cudaMemcpyDefault, s);
+    KVOFF_TRY(cuda_status(e, "cudaMemcpy2DAsync (token copy)"));
+  }
+  return ok();
+}
+
 int kvoff_device_error(int32_t device, int32_t* flags, int32_t clear) {
   if (flags == nullptr) return fail(KVOFF_EINVAL, "kvoff_device_error: null output");
   int prev = 0;

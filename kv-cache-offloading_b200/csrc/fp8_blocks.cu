@@ -171,18 +171,36 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Dequantize 8 e4m3 (two packed words) with scale s into 8 bf16 (16 bytes).
+__device__ __forceinline__ uint4 dequantize8(const uint2 v, float s) {
+  const uint32_t pairs[4] = {v.x & 0xFFFFu, v.x >> 16, v.y & 0xFFFFu, v.y >> 16};
+  uint32_t out[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = e4m3x2_to_f32x2(pairs[j]);
+    out[j] = f32x2_to_bf16x2(__fmul_rn(f.x, s), __fmul_rn(f.y, s));
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// LANES lanes own one row of D = 16 * LANES elements; lane li handles the two
+// 8-element pieces at li * 8 and D / 2 + li * 8 (8-byte payload loads, 16-byte
+// bf16 stores, each warp instruction contiguous within a row). kRowGroups row
+// groups are loaded first: 8 independent 8-byte loads per lane in flight, which
+// this latency-bound kernel needs to keep HBM busy.
 template <int LANES>
 __global__ void __launch_bounds__(kThreads)
     fp8_restore_kernel(uint16_t* __restrict__ pool, const Geometry g,
                        const __grid_constant__ BlockTable t, int64_t units) {
   constexpr int kRowsPerWarp = 32 / LANES;
   constexpr int kRowsPerIter = kRowsPerWarp * kWarps;
+  constexpr int kRowGroups = 4;
+  constexpr int D = 16 * LANES;
   __shared__ uint16_t s_scale[kTile];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int sub = lane / LANES;
   const int li = lane % LANES;
-  const int D = 8 * LANES;
 
   for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
     const Unit un = decode_unit(u, g, t);
@@ -191,27 +209,27 @@ __global__ void __launch_bounds__(kThreads)
     uint16_t* dst = pool + un.pool_elem;
     for (int j = threadIdx.x; j < un.rows; j += kThreads) s_scale[j] = ssrc[j];
     __syncthreads();
-    for (int base = 0; base < un.rows; base += kRowsPerIter * kUnroll) {
-      uint2 v[kUnroll];
+    for (int base = 0; base < un.rows; base += kRowsPerIter * kRowGroups) {
+      uint2 v[kRowGroups][2];
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
+      for (int k = 0; k < kRowGroups; ++k) {
         const int r = base + k * kRowsPerIter + warp * kRowsPerWarp + sub;
-        v[k] = r < un.rows ? ld_stream8(psrc + (int64_t)r * D + li * 8) : make_uint2(0, 0);
+        if (r < un.rows) {
+          const uint8_t* row = psrc + (int64_t)r * D + li * 8;
+          v[k][0] = ld_stream8(row);
+          v[k][1] = ld_stream8(row + D / 2);
+        } else {
+          v[k][0] = v[k][1] = make_uint2(0, 0);
+        }
       }
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
+      for (int k = 0; k < kRowGroups; ++k) {
         const int r = base + k * kRowsPerIter + warp * kRowsPerWarp + sub;
         if (r >= un.rows) continue;
         const float s = bf16_to_f32(s_scale[r]);
-        const uint32_t pairs[4] = {v[k].x & 0xFFFFu, v[k].x >> 16, v[k].y & 0xFFFFu, v[k].y >> 16};
-        uint32_t out[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = e4m3x2_to_f32x2(pairs[j]);
-          out[j] = f32x2_to_bf16x2(__fmul_rn(f.x, s), __fmul_rn(f.y, s));
-        }
-        *reinterpret_cast<uint4*>(dst + (int64_t)r * D + li * 8) =
-            make_uint4(out[0], out[1], out[2], out[3]);
+        uint16_t* out = dst + (int64_t)r * D + li * 8;
+        *reinterpret_cast<uint4*>(out) = dequantize8(v[k][0], s);
+        *reinterpret_cast<uint4*>(out + D / 2) = dequantize8(v[k][1], s);
       }
     }
     __syncthreads();
@@ -300,9 +318,9 @@ int validate(Args& a, int64_t num_chunks, int64_t chunk_stride, int64_t block_st
 
 bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
 
-// Lanes per row for the vectorized kernels, or 0 for the generic path. A save
-// lane handles 16 elements of a row, a restore lane 8.
-int vector_lanes(const Args& a, void* const* payload, void* const* scale, bool save) {
+// Lanes per row for the vectorized kernels (16 elements per lane), or 0 for
+// the generic path.
+int vector_lanes(const Args& a, void* const* payload, void* const* scale) {
   int lanes = 0;
   switch (a.g.head_dim) {
     case 32: lanes = 4; break;
@@ -311,7 +329,7 @@ int vector_lanes(const Args& a, void* const* payload, void* const* scale, bool s
     case 256: lanes = 32; break;
     default: return 0;
   }
-  if (save) lanes /= 2;
+  lanes /= 2;  // each lane handles 16 elements of a row
   if (!aligned(a.pool, 16) || (a.g.chunk_stride % 8) != 0 || (a.g.block_stride % 8) != 0)
     return 0;
   for (int64_t i = 0; i < a.count; ++i)
@@ -331,10 +349,10 @@ const void* pick_kernel(int lanes) {
     }
   }
   switch (lanes) {
+    case 2: return (const void*)fp8_restore_kernel<2>;
     case 4: return (const void*)fp8_restore_kernel<4>;
     case 8: return (const void*)fp8_restore_kernel<8>;
     case 16: return (const void*)fp8_restore_kernel<16>;
-    case 32: return (const void*)fp8_restore_kernel<32>;
     default: return (const void*)fp8_restore_generic_kernel;
   }
 }
@@ -346,7 +364,7 @@ int launch(const Args& a, void* const* payload, void* const* scale, int32_t max_
   for (int64_t i = 0; i < a.count; ++i)
     if (payload[i] == nullptr || scale[i] == nullptr)
       return fail(KVOFF_EINVAL, "kvoff_%s: null slot pointer at %lld", a.op, (long long)i);
-  const int lanes = vector_lanes(a, payload, scale, kSave);
+  const int lanes = vector_lanes(a, payload, scale);
   const void* kernel = pick_kernel<kSave>(lanes);
   for (int64_t first = 0; first < a.count; first += kMaxBatch) {
     const int n = (int)((a.count - first) < kMaxBatch ? (a.count - first) : kMaxBatch);
@@ -368,10 +386,10 @@ int launch(const Args& a, void* const* payload, void* const* scale, int32_t max_
         }
       } else {
         switch (lanes) {
+          case 2: fp8_restore_kernel<2><<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, units); break;
           case 4: fp8_restore_kernel<4><<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, units); break;
           case 8: fp8_restore_kernel<8><<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, units); break;
-          case 16: fp8_restore_kernel<16><<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, units); break;
-          default: fp8_restore_kernel<32><<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, units); break;
+          default: fp8_restore_kernel<16><<<grid, kThreads, 0, stream>>>((uint16_t*)a.pool, a.g, t, units); break;
         }
       }
     } else {

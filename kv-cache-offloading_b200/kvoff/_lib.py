@@ -42,6 +42,8 @@ SIGNATURES = {
                                                        _PI64, _I64, _PP, _PP, _P, _P, _I64, _P]),
     "kvoff_copy_blocks": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _PI64, _I64, _PP, _I32,
                                          _I32, _I32, _P]),
+    "kvoff_copy_tokens": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _PI64, _I64, _P,
+                                         _I32, _P]),
     "kvoff_store_kvcache": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _I64, _I64, _P,
                                            _P]),
     "kvoff_host_alloc": (ctypes.c_int, [ctypes.c_uint64, _I32, _PP, _PP]),

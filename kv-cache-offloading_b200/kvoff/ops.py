@@ -182,6 +182,23 @@ def copy_blocks(pool: torch.Tensor, block_ids, slot_ptrs, *, restore: bool = Fal
                   max_ctas, _stream(pool.device, stream))
 
 
+def copy_tokens(pool: torch.Tensor, block_ids, num_tokens: int, dense_ptr: int, *,
+                restore: bool = False, stream=None) -> None:
+    """Tokens [0, num_tokens) of a sequence's blocks <-> dense [2, L, num_tokens, H, D]."""
+    _require_cuda(pool, "pool")
+    g = geometry(pool)
+    block_size = pool.shape[3]
+    token_bytes = pool.shape[4] * pool.shape[5] * g.elem_size
+    needed = -(-num_tokens // block_size)
+    if len(block_ids) < needed:
+        raise ValueError("sequence is missing KV blocks")
+    with torch.cuda.device(pool.device):
+        _lib.call("kvoff_copy_tokens", pool.data_ptr(), g.num_chunks, g.chunk_stride * g.elem_size,
+                  g.block_stride * g.elem_size, g.num_blocks, block_size, token_bytes,
+                  _lib.int64_array(block_ids[:needed]), int(num_tokens), int(dense_ptr),
+                  _lib.RESTORE if restore else _lib.SAVE, _stream(pool.device, stream))
+
+
 def memcpy(dst_ptr: int, src_ptr: int, nbytes: int, *, device, stream=None) -> None:
     """cudaMemcpyAsync(cudaMemcpyDefault) on `stream`."""
     device = torch.device(device)

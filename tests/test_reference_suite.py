@@ -1,9 +1,10 @@
-"""Run the reference project's own test suite against the drop-in module.
+"""Run the reference project's own test suite against the drop-in modules.
 
-A temporary copy of the reference tree gets kvoff's cpu_prefix_cache.py in
-place of nanovllm/engine/cpu_prefix_cache.py, then the reference's pytest
-suite runs unmodified (its CUDA cases skip without a GPU). Skipped when the
-reference checkout is not available (set KVOFF_REFERENCE to point at it).
+A temporary copy of the reference tree gets kvoff's cpu_prefix_cache.py and
+kv_handoff.py in place of nanovllm/engine/cpu_prefix_cache.py and
+nanovllm/engine/kv_handoff.py, then the reference's pytest suite runs
+unmodified (its CUDA cases skip without a GPU). Skipped when the reference
+checkout is not available (set KVOFF_REFERENCE to point at it).
 """
 
 from __future__ import annotations
@@ -19,7 +20,9 @@ import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 REFERENCE = Path(os.environ.get("KVOFF_REFERENCE", "/root/reference"))
-DROPIN = ROOT / "kv-cache-offloading_b200" / "kvoff" / "cpu_prefix_cache.py"
+KVOFF = ROOT / "kv-cache-offloading_b200" / "kvoff"
+DROPINS = {"cpu_prefix_cache.py": KVOFF / "cpu_prefix_cache.py",
+           "kv_handoff.py": KVOFF / "kv_handoff.py"}
 
 
 @pytest.mark.skipif(not (REFERENCE / "bench").is_dir(), reason="reference checkout not present")
@@ -28,8 +31,9 @@ def test_reference_suite_passes_with_the_dropin(tmp_path):
     shutil.copytree(REFERENCE / "bench", tree / "bench")
     shutil.copytree(REFERENCE / "nanovllm_upstream", tree / "nanovllm_upstream",
                     ignore=shutil.ignore_patterns("assets", "*.png"))
-    target = tree / "nanovllm_upstream" / "nanovllm" / "engine" / "cpu_prefix_cache.py"
-    shutil.copyfile(DROPIN, target)
+    engine = tree / "nanovllm_upstream" / "nanovllm" / "engine"
+    for name, source in DROPINS.items():
+        shutil.copyfile(source, engine / name)
     env = dict(os.environ, PYTHONPATH=os.pathsep.join(
         [str(tree), str(ROOT / "kv-cache-offloading_b200")]), PYTHONDONTWRITEBYTECODE="1")
     result = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider",
