@@ -30,7 +30,6 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kTile = 256;       // rows per unit
 constexpr int kMaxBatch = 128;   // blocks per launch (kernel-parameter table)
-constexpr int kUnroll = 4;       // independent 16-byte loads in flight per lane
 
 struct Geometry {
   int64_t num_chunks;      // 2 * layers

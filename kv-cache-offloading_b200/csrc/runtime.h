@@ -6,7 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/kvoff.h"
+#include "kvoff.h"
 
 namespace kvoff {
 
