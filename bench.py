@@ -117,6 +117,8 @@ def parse_args():
     p.add_argument("--slab-gib", type=float, default=24.0, help="pinned host slab per GPU")
     p.add_argument("--no-sweep", action="store_true", help="skip the batch-size / mode sweep")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-dropin", action="store_true",
+                   help="skip the per-block vs batched CPUBlockCache measurement")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
     args = p.parse_args()
     if args.warmup < 3:
@@ -364,6 +366,68 @@ def max_over_ranks(torch, value: float, device) -> float:
     return float(t.item())
 
 
+class _Block:
+    def __init__(self, block_id: int):
+        self.block_id, self.hash, self.token_ids = block_id, -1, []
+
+
+def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, main) -> dict:
+    """FP8 save + restore of the step's blocks through the drop-in CPUBlockCache.
+
+    per_block: one save_block / _copy_entry per block, the block manager's call
+    pattern; batched: one save_blocks and one _copy_entries per step. The step
+    joins both copy streams into the timing stream; each step discards the saved
+    entries so that the next step saves them again.
+    """
+    from types import SimpleNamespace
+
+    from kvoff.cpu_prefix_cache import CPUBlockCache
+
+    B = len(save_ids)
+    blocks = [_Block(i) for i in range(w.num_blocks)]
+    manager = SimpleNamespace(blocks=blocks, block_size=w.block_size, hash_to_block_id={},
+                              _cpu_prefix_cache=None, admission_blocked=False)
+    runner = SimpleNamespace(world_size=1, block_size=w.block_size, kv_cache=pool)
+    cache = CPUBlockCache(runner, manager, 2 * B * (w.fp8_block + 4096), split_streams=True,
+                          fp8=True, preallocate=True)
+
+    def publish(block_id: int, tag: int) -> int:
+        h = 1_000_000 + tag
+        blocks[block_id].hash, blocks[block_id].token_ids = h, [tag] * w.block_size
+        manager.hash_to_block_id[h] = block_id
+        return h
+
+    saves = [publish(b, i) for i, b in enumerate(save_ids)]
+    sources = [publish(b, B + i) for i, b in enumerate(restore_ids)]
+    cache.save_blocks(sources)
+    entries = [cache._entries[h] for h in sources]
+    cache.synchronize()
+
+    def join():
+        main.wait_stream(cache._copy_stream)
+        main.wait_stream(cache._restore_stream)
+        for h in saves:
+            cache.discard(h)
+
+    def per_block():
+        for h, e, b in zip(saves, entries, restore_ids):
+            cache.save_block(h)
+            cache._copy_entry(e, b, wait=False)
+        join()
+
+    def batched():
+        cache.save_blocks(saves)
+        cache._copy_entries(entries, restore_ids, wait=False)
+        join()
+
+    out = {}
+    for name, step in (("per_block", per_block), ("batched", batched)):
+        ms = timer.run(step, args.steps, args.warmup) / args.steps
+        out[name] = 2 * B * w.bf16_block / (ms / 1e3) / 1e9
+    cache.close()
+    return out
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -607,6 +671,10 @@ def run_ours(args) -> None:
     launches = (launches_per_call if save_mode == "mapped" else groups) + \
         (launches_per_call if restore_mode == "mapped" else groups)
 
+    # ---- through the drop-in CPUBlockCache: per-block calls vs batched calls ----
+    dropin = dropin_e2e(torch, w, pool, save_ids, restore_ids, args, timer, main) \
+        if w.batch <= 256 and not args.no_dropin else None
+
     # ---- PCIe ceiling: pinned memcpy per direction and duplex -------------------
     blocks = min(B, 64, max(1, int(2.5e9 // w.fp8_block)))
     n_bytes = blocks * w.fp8_block
@@ -685,6 +753,7 @@ def run_ours(args) -> None:
         "gpu_launches": launches * args.steps,
         "pcie_memcpy_ceiling_GBps": ceiling,
         "sweep_GBps": sweep,
+        "dropin_e2e_GBps": dropin,
         "reference_gpu_path": ref_gpu,
     }
     if rank == 0:

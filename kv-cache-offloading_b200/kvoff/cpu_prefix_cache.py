@@ -162,6 +162,7 @@ class CPUBlockCache:
             if fp8 and pool.dtype != torch.bfloat16:
                 raise ValueError("fp8=True needs a bf16 KV pool")
             self._modes = _transfer_modes()
+            self._staging_blocks = max(1, int(os.environ.get("KVOFF_STAGING_BLOCKS", "2")))
             self._copy_stream = torch.cuda.Stream(pool.device)
             self._restore_stream = (torch.cuda.Stream(pool.device) if split_streams
                                     else self._copy_stream)
@@ -280,19 +281,17 @@ class CPUBlockCache:
         return self._slabs[chunk][index], self._scale_slabs[chunk][index] if self._fp8 else None
 
     def _stage(self, stream) -> tuple[torch.Tensor, torch.Tensor | None]:
-        """Per-stream device staging (FP8 payload + scales, or one raw block).
-
-        Work on one stream runs in order, so reusing its staging is safe.
+        """Per-stream device staging of _staging_blocks blocks (FP8 payloads +
+        scales, or raw blocks). Work on one stream runs in order, so reusing its
+        staging is safe; with two or more blocks the staged FP8 calls overlap the
+        quantize kernels of one block with the DMA of the previous one.
         """
         if stream not in self._staging:
-            device = self._cache.device
-            if self._fp8:
-                self._staging[stream] = (
-                    torch.empty(self._payload_bytes, dtype=torch.uint8, device=device),
-                    torch.empty(self._scale_bytes, dtype=torch.uint8, device=device))
-            else:
-                self._staging[stream] = (
-                    torch.empty(self._payload_bytes, dtype=torch.uint8, device=device), None)
+            device, n = self._cache.device, self._staging_blocks
+            scales = (torch.empty((n, self._scale_bytes), dtype=torch.uint8, device=device)
+                      if self._fp8 else None)
+            self._staging[stream] = (
+                torch.empty((n, self._payload_bytes), dtype=torch.uint8, device=device), scales)
         return self._staging[stream]
 
     # -- device copies (CUDA pools) ---------------------------------------------
@@ -307,61 +306,67 @@ class CPUBlockCache:
         return (owner.device_alias(payload),
                 owner.device_alias(scale) if scale is not None else 0)
 
-    def _device_save(self, pool: torch.Tensor, block_id: int, slot: int, stream):
-        """Enqueue pool block -> slot on `stream` (the current stream inside)."""
+    def _pointers(self, slots, mapped: bool) -> tuple[list[int], list[int]]:
+        pairs = [self._slot_pointers(slot, mapped) for slot in slots]
+        return [p for p, _ in pairs], [s for _, s in pairs]
+
+    def _device_save(self, pool: torch.Tensor, block_ids, slots, stream):
+        """Enqueue pool blocks -> slots on `stream` (one native call per method)."""
         ops, modes = self._ops, self._modes
         if self._fp8:
             mapped = modes["fp8_save"] == "mapped"
-            payload, scale = self._slot_pointers(slot, mapped)
+            payload, scale = self._pointers(slots, mapped)
             if mapped:
-                ops.save_fp8(pool, [block_id], [payload], [scale], stream=stream)
+                ops.save_fp8(pool, block_ids, payload, scale, stream=stream)
             else:
-                staged, staged_scale = self._stage(stream)
-                ops.save_fp8_staged(pool, [block_id], [payload], [scale], staged, staged_scale,
+                ops.save_fp8_staged(pool, block_ids, payload, scale, *self._stage(stream),
                                     stream=stream)
             return
         method = modes["bf16_save"]
-        payload, _ = self._slot_pointers(slot, method == "sm")
+        payload, _ = self._pointers(slots, method == "sm")
         if method == "tma":
             staged, _ = self._stage(stream)
-            ops.copy_blocks(pool, [block_id], [staged.data_ptr()], method=ops.COPY_TMA,
-                            stream=stream)
-            ops.memcpy(payload, staged.data_ptr(), self._payload_bytes, device=pool.device,
-                       stream=stream)
+            for first in range(0, len(block_ids), len(staged)):
+                ids = block_ids[first:first + len(staged)]
+                ops.copy_blocks(pool, ids, [staged[i].data_ptr() for i in range(len(ids))],
+                                method=ops.COPY_TMA, stream=stream)
+                for i in range(len(ids)):
+                    ops.memcpy(payload[first + i], staged[i].data_ptr(), self._payload_bytes,
+                               device=pool.device, stream=stream)
         else:
-            ops.copy_blocks(pool, [block_id], [payload], stream=stream,
+            ops.copy_blocks(pool, block_ids, payload, stream=stream,
                             method=ops.COPY_SM if method == "sm" else ops.COPY_ENGINE)
 
-    def _device_restore(self, pool: torch.Tensor, block_id: int, payload: int, scale: int,
-                        mapped_payload: int, mapped_scale: int, stream):
-        """Enqueue slot -> pool block on `stream`."""
+    def _device_restore(self, pool: torch.Tensor, block_ids, plain, mapped, stream):
+        """Enqueue slots -> pool blocks on `stream`; plain / mapped are the slots'
+        (payload, scale) host pointers and device aliases."""
         ops, modes = self._ops, self._modes
         if self._fp8:
             if modes["fp8_restore"] == "mapped":
-                ops.restore_fp8(pool, [block_id], [mapped_payload], [mapped_scale], stream=stream)
+                ops.restore_fp8(pool, block_ids, *mapped, stream=stream)
             else:
-                staged, staged_scale = self._stage(stream)
-                ops.restore_fp8_staged(pool, [block_id], [payload], [scale], staged,
-                                       staged_scale, stream=stream)
+                ops.restore_fp8_staged(pool, block_ids, *plain, *self._stage(stream),
+                                       stream=stream)
             return
         method = modes["bf16_restore"]
         if method == "tma":
             staged, _ = self._stage(stream)
-            ops.memcpy(staged.data_ptr(), payload, self._payload_bytes, device=pool.device,
-                       stream=stream)
-            ops.copy_blocks(pool, [block_id], [staged.data_ptr()], restore=True,
-                            method=ops.COPY_TMA, stream=stream)
+            for first in range(0, len(block_ids), len(staged)):
+                ids = block_ids[first:first + len(staged)]
+                for i in range(len(ids)):
+                    ops.memcpy(staged[i].data_ptr(), plain[0][first + i], self._payload_bytes,
+                               device=pool.device, stream=stream)
+                ops.copy_blocks(pool, ids, [staged[i].data_ptr() for i in range(len(ids))],
+                                restore=True, method=ops.COPY_TMA, stream=stream)
         elif method == "sm":
-            ops.copy_blocks(pool, [block_id], [mapped_payload], restore=True,
-                            method=ops.COPY_SM, stream=stream)
+            ops.copy_blocks(pool, block_ids, mapped[0], restore=True, method=ops.COPY_SM,
+                            stream=stream)
         else:
-            ops.copy_blocks(pool, [block_id], [payload], restore=True, stream=stream)
+            ops.copy_blocks(pool, block_ids, plain[0], restore=True, stream=stream)
 
-    def _restore_slot(self, slot: int, block_id: int, stream):
-        mapped = self._slot_pointers(slot, True)
-        plain = self._slot_pointers(slot, False)
-        self._device_restore(self._cache, block_id, plain[0], plain[1], mapped[0], mapped[1],
-                             stream)
+    def _restore_slots(self, slots, block_ids, stream):
+        self._device_restore(self._cache, block_ids, self._pointers(slots, False),
+                             self._pointers(slots, True), stream)
 
     # -- host copies (CPU pools: the reference's synchronous path) ---------------
 
@@ -406,10 +411,10 @@ class CPUBlockCache:
             with torch.cuda.stream(stream):
                 start.record(stream)
                 for i in range(repeats):
-                    p, s = payload[i].data_ptr(), scale[i].data_ptr() if scale is not None else 0
-                    self._device_restore(scratch_pool, 0, p, s, slab.device_alias(payload[i]),
-                                         slab.device_alias(scale[i]) if scale is not None else 0,
-                                         stream)
+                    s_ptr = scale[i].data_ptr() if scale is not None else 0
+                    s_alias = slab.device_alias(scale[i]) if scale is not None else 0
+                    self._device_restore(scratch_pool, [0], ([payload[i].data_ptr()], [s_ptr]),
+                                         ([slab.device_alias(payload[i])], [s_alias]), stream)
                 end.record(stream)
             end.synchronize()
         return start.elapsed_time(end) / 1000 / repeats
@@ -451,7 +456,7 @@ class CPUBlockCache:
         try:
             payload, scale = self._slot_view(slot)
             if self._on_cuda:
-                done = self._save_on_device(block_id, slot)
+                done = self._save_on_device([block_id], [slot])
             else:
                 self._host_save(self._cache[:, :, block_id], payload, scale)
         except BaseException:
@@ -461,22 +466,79 @@ class CPUBlockCache:
         self._saved_blocks += 1
         return True
 
-    def _save_on_device(self, block_id: int, slot: int) -> torch.cuda.Event:
+    @torch.inference_mode()
+    def save_blocks(self, prefix_hashes) -> list[bool]:
+        """Save several published full blocks with one copy call; True per new save.
+
+        Each hash follows save_block's rules (KeyError, ValueError, False when
+        already saved). The batch is checked in full - keys, metadata, budget -
+        before any slot is taken, and a failed copy saves none of it. On CUDA
+        the blocks move in one native call and share one completion event,
+        instead of one launch, one DMA pair and one event per block.
+        """
+        self._require_open()
+        todo, results, seen = [], [], set()
+        for prefix_hash in prefix_hashes:
+            entry = self._entries.get(prefix_hash)
+            block_id = self._manager.hash_to_block_id.get(prefix_hash)
+            if block_id is None:
+                if entry is not None:
+                    results.append(False)
+                    continue
+                raise KeyError(f"GPU prefix block {prefix_hash} is not cached")
+            block = self._manager.blocks[block_id]
+            tokens = tuple(block.token_ids)
+            if block.hash != prefix_hash or len(tokens) != self._manager.block_size:
+                raise ValueError("source must be a published full prefix block")
+            if entry is not None and entry.token_ids != tokens:
+                raise ValueError("prefix hash has conflicting token metadata")
+            new = entry is None and prefix_hash not in seen
+            results.append(new)
+            if new:
+                seen.add(prefix_hash)
+                todo.append((prefix_hash, block_id, tokens))
+        if not todo:
+            return results
+        if self.bytes_used + len(todo) * self._block_bytes > self._max_bytes:
+            raise CPUCacheFullError("CPU prefix cache payload budget exceeded")
+        while len(self._free_slots) < len(todo) and self._num_slots < self._capacity:
+            self._grow()
+        slots = [self._free_slots.pop() for _ in todo]
+        done = None
+        try:
+            if self._on_cuda:
+                done = self._save_on_device([b for _, b, _ in todo], slots)
+            else:
+                for (_, block_id, _), slot in zip(todo, slots):
+                    payload, scale = self._slot_view(slot)
+                    self._host_save(self._cache[:, :, block_id], payload, scale)
+        except BaseException:
+            self._free_slots.extend(reversed(slots))
+            raise
+        for (prefix_hash, _, tokens), slot in zip(todo, slots):
+            payload, scale = self._slot_view(slot)
+            self._entries[prefix_hash] = _CPUBlock(tokens, payload, slot, scale, done)
+        self._saved_blocks += len(todo)
+        return results
+
+    def _save_on_device(self, block_ids, slots) -> torch.cuda.Event:
         pool = self._cache
         current = torch.cuda.current_stream(pool.device)
         copy = self._copy_stream
-        # After the kernels that wrote the block; with split streams also after
-        # earlier restores that read this slot. before_block_reuse orders the
+        # After the kernels that wrote the blocks; with split streams also after
+        # earlier restores that read these slots. before_block_reuse orders each
         # block's next writer after the returned event.
         copy.wait_stream(current)
-        read = self._slot_reads.pop(slot, None)
-        if read is not None and self._restore_stream is not copy:
-            copy.wait_event(read)
+        for slot in slots:
+            read = self._slot_reads.pop(slot, None)
+            if read is not None and self._restore_stream is not copy:
+                copy.wait_event(read)
         with torch.cuda.stream(copy):
-            self._device_save(pool, block_id, slot, copy)
+            self._device_save(pool, list(block_ids), list(slots), copy)
             done = torch.cuda.Event()
             done.record(copy)
-        self._pending_saves[block_id] = done
+        for block_id in block_ids:
+            self._pending_saves[block_id] = done
         return done
 
     def _preserve(self, prefix_hash: int):
@@ -533,7 +595,7 @@ class CPUBlockCache:
         if entry.saved is not None and stream is not self._copy_stream:
             stream.wait_event(entry.saved)
         with torch.cuda.stream(stream):
-            self._restore_slot(entry.slot, block_id, stream)
+            self._restore_slots([entry.slot], [block_id], stream)
             done = torch.cuda.Event()
             done.record(stream)
         self._slot_reads[entry.slot] = done
@@ -542,6 +604,48 @@ class CPUBlockCache:
         else:
             self._pending_restores[block_id] = done
         self._restored_blocks += 1
+
+    @torch.inference_mode()
+    def _copy_entries(self, entries, block_ids, wait: bool = True):
+        """_copy_entry for several entries with one copy call and one event.
+
+        For callers that restore a run of blocks at once (an admission's CPU
+        hits, a prefetch): the same ordering as _copy_entry per block, with the
+        copies issued as one native call on the restore stream.
+        """
+        self._require_open()
+        entries, block_ids = list(entries), list(block_ids)
+        if len(entries) != len(block_ids):
+            raise ValueError("one target block per entry")
+        if not entries:
+            return
+        if not self._on_cuda:
+            for entry, block_id in zip(entries, block_ids):
+                self._host_restore(entry, self._cache[:, :, block_id])
+            self._restored_blocks += len(entries)
+            return
+        pool = self._cache
+        current = torch.cuda.current_stream(pool.device)
+        stream = self._restore_stream
+        stream.wait_stream(current)
+        if stream is not self._copy_stream:
+            waited = set()
+            for entry in entries:
+                if entry.saved is not None and id(entry.saved) not in waited:
+                    waited.add(id(entry.saved))
+                    stream.wait_event(entry.saved)
+        with torch.cuda.stream(stream):
+            self._restore_slots([e.slot for e in entries], block_ids, stream)
+            done = torch.cuda.Event()
+            done.record(stream)
+        for entry in entries:
+            self._slot_reads[entry.slot] = done
+        if wait:
+            current.wait_event(done)
+        else:
+            for block_id in block_ids:
+                self._pending_restores[block_id] = done
+        self._restored_blocks += len(entries)
 
     @torch.inference_mode()
     def restore_block(self, prefix_hash: int) -> int:

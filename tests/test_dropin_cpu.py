@@ -284,3 +284,45 @@ def test_reference_quality_harness_slice_still_loads():
     out = torch.empty_like(x)
     namespace["fp8_dequantize"](payload, scale, out)
     assert np.array_equal(bits_u16(out), golden["deq_128"])
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_batched_save_and_restore_match_per_block_calls(fp8):
+    shape = (2, 2, 8, 256, 1, 4)
+    pools = [finite_pool(shape) for _ in range(2)]
+    outs = []
+    for batched, pool in zip((False, True), pools):
+        engine = FakeEngine(pool)
+        m = engine.manager
+        keys = [m.publish(b) for b in (5, 1, 6)]
+        cache = engine.create_cpu_prefix_cache(8 * per_block(pool), fp8=fp8)
+        if batched:
+            assert cache.save_blocks(keys + [keys[0]]) == [True, True, True, False]
+            assert cache.save_blocks(keys) == [False, False, False]
+        else:
+            assert all(cache.save_block(k) for k in keys)
+        entries = [cache._entries[k] for k in keys]
+        if batched:
+            cache._copy_entries(entries, [0, 2, 3])
+        else:
+            for e, b in zip(entries, [0, 2, 3]):
+                cache._copy_entry(e, b)
+        outs.append((bits_u16(pool), [e.kv.view(torch.uint8).clone() for e in entries]))
+        assert cache.stats["saved_blocks"] == 3 and cache.stats["restored_blocks"] == 3
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert all(torch.equal(a, b) for a, b in zip(outs[0][1], outs[1][1]))
+
+
+def test_batched_save_is_all_or_nothing():
+    engine = FakeEngine(arbitrary_pool())
+    m = engine.manager
+    keys = [m.publish(b) for b in (0, 1, 2)]
+    cache = engine.create_cpu_prefix_cache(2 * per_block(engine.pool))
+    with pytest.raises(MemoryError, match="budget"):
+        cache.save_blocks(keys)
+    assert len(cache) == 0 and cache.reserved_bytes == 0
+    with pytest.raises(KeyError):
+        cache.save_blocks([keys[0], 12345])
+    assert len(cache) == 0
+    assert cache.save_blocks(keys[:2]) == [True, True]
+    assert cache.bytes_used == 2 * cache.block_bytes

@@ -244,3 +244,57 @@ def test_prefetch_restore_orders_first_use(cuda):
     m.acquire_block(target)  # first reader: waits for the pending restore
     got = engine.pool[:, :, target].contiguous().view(torch.uint8).cpu()
     assert torch.equal(got, expected)
+
+
+@pytest.mark.parametrize("modes", [("staged", "engine"), ("mapped", "sm"), ("staged", "tma")])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_batched_calls_match_per_block_calls(cuda, monkeypatch, modes, fp8):
+    fp8_mode, bf16_mode = modes
+    for key in ("KVOFF_FP8_SAVE", "KVOFF_FP8_RESTORE"):
+        monkeypatch.setenv(key, fp8_mode)
+    for key in ("KVOFF_BF16_SAVE", "KVOFF_BF16_RESTORE"):
+        monkeypatch.setenv(key, bf16_mode)
+    shape = (2, 3, 10, 256, 8, 128)
+    results = []
+    for batched in (False, True):
+        engine = FakeEngine(finite_pool(shape, cuda, seed=4))
+        m = engine.manager
+        keys = [m.publish(b) for b in (9, 2, 5, 7)]
+        cache = engine.create_cpu_prefix_cache(6 * per_block(engine.pool), fp8=fp8,
+                                               split_streams=True)
+        if batched:
+            assert cache.save_blocks(keys) == [True] * 4
+        else:
+            assert all(cache.save_block(k) for k in keys)
+        entries = [cache._entries[k] for k in keys]
+        targets = [0, 1, 3, 4]
+        if batched:
+            cache._copy_entries(entries, targets, wait=False)
+        else:
+            for e, b in zip(entries, targets):
+                cache._copy_entry(e, b, wait=False)
+        for b in targets:
+            cache.before_block_use(b)
+        cache.synchronize()
+        results.append((bits_u16(engine.pool),
+                        [e.kv.view(torch.uint8).clone() for e in entries]))
+    assert np.array_equal(results[0][0], results[1][0])
+    assert all(torch.equal(a, b) for a, b in zip(results[0][1], results[1][1]))
+
+
+def test_batched_restore_waits_for_its_saves(cuda):
+    engine = FakeEngine(arbitrary_pool((2, 3, 8, 256, 8, 128), cuda))
+    m = engine.manager
+    keys = [m.publish(b) for b in (1, 2, 3)]
+    expected = [block_bytes(engine.pool, b) for b in (1, 2, 3)]
+    cache = engine.create_cpu_prefix_cache(3 * per_block(engine.pool), split_streams=True,
+                                           preallocate=True)
+    for slab in cache._slabs:
+        slab.view(torch.uint8).fill_(0xAB)
+    with torch.cuda.stream(cache._copy_stream):
+        torch.cuda._sleep(SLEEP_CYCLES)
+    assert cache.save_blocks(keys) == [True] * 3
+    cache._copy_entries([cache._entries[k] for k in keys], [5, 6, 7])
+    cache.synchronize()
+    for b, want in zip((5, 6, 7), expected):
+        assert torch.equal(block_bytes(engine.pool, b), want)
