@@ -424,6 +424,10 @@ def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, mai
     for name, step in (("per_block", per_block), ("batched", batched)):
         ms = timer.run(step, args.steps, args.warmup) / args.steps
         out[name] = 2 * B * w.bf16_block / (ms / 1e3) / 1e9
+    # The hybrid planner's restore cost at the batch sizes admission restores.
+    out["restore_ms_per_block"] = {
+        str(b): 1e3 * cache.measure_restore_s_per_block(repeats=max(1, 64 // b), batch=b)
+        for b in SWEEP_BATCHES if b <= B}
     cache.close()
     return out
 

@@ -163,6 +163,8 @@ class CPUBlockCache:
                 raise ValueError("fp8=True needs a bf16 KV pool")
             self._modes = _transfer_modes()
             self._staging_blocks = max(1, int(os.environ.get("KVOFF_STAGING_BLOCKS", "2")))
+            self._batch_staging_blocks = max(
+                1, int(os.environ.get("KVOFF_BATCH_STAGING_BLOCKS", "8")))
             self._copy_stream = torch.cuda.Stream(pool.device)
             self._restore_stream = (torch.cuda.Stream(pool.device) if split_streams
                                     else self._copy_stream)
@@ -280,19 +282,26 @@ class CPUBlockCache:
         chunk, index = self._locate(slot)
         return self._slabs[chunk][index], self._scale_slabs[chunk][index] if self._fp8 else None
 
-    def _stage(self, stream) -> tuple[torch.Tensor, torch.Tensor | None]:
-        """Per-stream device staging of _staging_blocks blocks (FP8 payloads +
-        scales, or raw blocks). Work on one stream runs in order, so reusing its
-        staging is safe; with two or more blocks the staged FP8 calls overlap the
-        quantize kernels of one block with the DMA of the previous one.
+    def _stage(self, stream, blocks: int = 0) -> tuple[torch.Tensor, torch.Tensor | None]:
+        """Per-stream device staging (FP8 payloads + scales, or raw blocks).
+
+        Work on one stream runs in order, so reusing its staging is safe. It
+        holds _staging_blocks blocks (2 by default: the staged FP8 calls then
+        overlap the kernel of one block with the DMA of the previous one); a
+        batched call grows it to min(blocks, _batch_staging_blocks) so a run of
+        blocks drains in few, large DMA copies. A replaced buffer is released
+        in stream order, after every copy that used it.
         """
-        if stream not in self._staging:
-            device, n = self._cache.device, self._staging_blocks
-            scales = (torch.empty((n, self._scale_bytes), dtype=torch.uint8, device=device)
+        want = max(self._staging_blocks, min(blocks, self._batch_staging_blocks))
+        staged = self._staging.get(stream)
+        if staged is None or staged[0].shape[0] < want:
+            device = self._cache.device
+            scales = (torch.empty((want, self._scale_bytes), dtype=torch.uint8, device=device)
                       if self._fp8 else None)
-            self._staging[stream] = (
-                torch.empty((n, self._payload_bytes), dtype=torch.uint8, device=device), scales)
-        return self._staging[stream]
+            staged = (torch.empty((want, self._payload_bytes), dtype=torch.uint8, device=device),
+                      scales)
+            self._staging[stream] = staged
+        return staged
 
     # -- device copies (CUDA pools) ---------------------------------------------
 
@@ -319,13 +328,13 @@ class CPUBlockCache:
             if mapped:
                 ops.save_fp8(pool, block_ids, payload, scale, stream=stream)
             else:
-                ops.save_fp8_staged(pool, block_ids, payload, scale, *self._stage(stream),
-                                    stream=stream)
+                ops.save_fp8_staged(pool, block_ids, payload, scale,
+                                    *self._stage(stream, len(block_ids)), stream=stream)
             return
         method = modes["bf16_save"]
         payload, _ = self._pointers(slots, method == "sm")
         if method == "tma":
-            staged, _ = self._stage(stream)
+            staged, _ = self._stage(stream, len(block_ids))
             for first in range(0, len(block_ids), len(staged)):
                 ids = block_ids[first:first + len(staged)]
                 ops.copy_blocks(pool, ids, [staged[i].data_ptr() for i in range(len(ids))],
@@ -345,12 +354,12 @@ class CPUBlockCache:
             if modes["fp8_restore"] == "mapped":
                 ops.restore_fp8(pool, block_ids, *mapped, stream=stream)
             else:
-                ops.restore_fp8_staged(pool, block_ids, *plain, *self._stage(stream),
-                                       stream=stream)
+                ops.restore_fp8_staged(pool, block_ids, *plain,
+                                       *self._stage(stream, len(block_ids)), stream=stream)
             return
         method = modes["bf16_restore"]
         if method == "tma":
-            staged, _ = self._stage(stream)
+            staged, _ = self._stage(stream, len(block_ids))
             for first in range(0, len(block_ids), len(staged)):
                 ids = block_ids[first:first + len(staged)]
                 for i in range(len(ids)):
@@ -385,24 +394,42 @@ class CPUBlockCache:
     # -- engine API -------------------------------------------------------------
 
     @torch.inference_mode()
-    def measure_restore_s_per_block(self, repeats: int = 8) -> float:
-        """Seconds per block of this cache's restore path (H2D, plus FP8 dequant)."""
+    def measure_restore_s_per_block(self, repeats: int = 8, batch: int = 1) -> float:
+        """Seconds per block of this cache's restore path (H2D, plus FP8 dequant).
+
+        batch > 1 times restores issued `batch` blocks per call (as _copy_entries
+        does for a run of CPU hits), so hybrid admission can use the per-block
+        cost at the batch size it actually restores; batch=1 is the per-block
+        call of _copy_entry.
+        """
         self._require_open()
         if not self._on_cuda:
             raise RuntimeError("restore timing needs a CUDA KV pool")
+        if repeats < 1 or batch < 1:
+            raise ValueError("repeats and batch must be positive")
         from kvoff.slab import PinnedSlab
 
         pool = self._cache
-        scratch_pool = torch.empty((2, pool.shape[1], 1, *pool.shape[3:]), dtype=pool.dtype,
+        scratch_pool = torch.empty((2, pool.shape[1], batch, *pool.shape[3:]), dtype=pool.dtype,
                                    device=pool.device)
-        scale_offset = -(-repeats * self._payload_bytes // 256) * 256
-        slab = PinnedSlab(scale_offset + repeats * self._scale_bytes, device=pool.device.index)
-        payload = slab.view(0, (repeats, self._payload_bytes), torch.uint8)
+        n = repeats * batch
+        scale_offset = -(-n * self._payload_bytes // 256) * 256
+        slab = PinnedSlab(scale_offset + n * self._scale_bytes, device=pool.device.index)
+        payload = slab.view(0, (n, self._payload_bytes), torch.uint8)
         payload.zero_()
         scale = None
         if self._fp8:
-            scale = slab.view(scale_offset, (repeats, self._scale_bytes // 2), pool.dtype)
+            scale = slab.view(scale_offset, (n, self._scale_bytes // 2), pool.dtype)
             scale.fill_(1.0)
+
+        def pointers(rows, alias):
+            ptr = slab.device_alias if alias else (lambda t: t.data_ptr())
+            return ([ptr(payload[i]) for i in rows],
+                    [ptr(scale[i]) if scale is not None else 0 for i in rows])
+
+        calls = [range(r * batch, (r + 1) * batch) for r in range(repeats)]
+        args = [(pointers(rows, False), pointers(rows, True)) for rows in calls]
+        targets = list(range(batch))
         stream = self._restore_stream
         stream.wait_stream(torch.cuda.current_stream(pool.device))
         for _ in range(2):  # the first pass warms up kernels and clocks
@@ -410,14 +437,11 @@ class CPUBlockCache:
             end = torch.cuda.Event(enable_timing=True)
             with torch.cuda.stream(stream):
                 start.record(stream)
-                for i in range(repeats):
-                    s_ptr = scale[i].data_ptr() if scale is not None else 0
-                    s_alias = slab.device_alias(scale[i]) if scale is not None else 0
-                    self._device_restore(scratch_pool, [0], ([payload[i].data_ptr()], [s_ptr]),
-                                         ([slab.device_alias(payload[i])], [s_alias]), stream)
+                for plain, mapped in args:
+                    self._device_restore(scratch_pool, targets, plain, mapped, stream)
                 end.record(stream)
             end.synchronize()
-        return start.elapsed_time(end) / 1000 / repeats
+        return start.elapsed_time(end) / 1000 / n
 
     def synchronize(self):
         """Wait for every pending host<->device copy (needed before host reads)."""

@@ -225,6 +225,10 @@ def test_measure_restore_s_per_block(cuda, fp8):
     cache = engine.create_cpu_prefix_cache(per_block(engine.pool), fp8=fp8, split_streams=True)
     seconds = cache.measure_restore_s_per_block(repeats=4)
     assert 0 < seconds < 1.0
+    batched = cache.measure_restore_s_per_block(repeats=2, batch=8)
+    assert 0 < batched < 1.0
+    with pytest.raises(ValueError):
+        cache.measure_restore_s_per_block(batch=0)
 
 
 def test_prefetch_restore_orders_first_use(cuda):
