@@ -117,6 +117,7 @@ def parse_args():
     p.add_argument("--slab-gib", type=float, default=24.0, help="pinned host slab per GPU")
     p.add_argument("--no-sweep", action="store_true", help="skip the batch-size / mode sweep")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-store", action="store_true", help="skip the store_kvcache measurement")
     p.add_argument("--no-dropin", action="store_true",
                    help="skip the per-block vs batched CPUBlockCache measurement")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
@@ -364,6 +365,55 @@ def max_over_ranks(torch, value: float, device) -> float:
     t = torch.tensor([value], dtype=torch.float64, device=device)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return float(t.item())
+
+
+def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict:
+    """Prefill slot store (BASELINE config 5 shape): 4096 new tokens per step for
+    each of the model's layers, scattered into non-contiguous free slots of the
+    pool, from K/V views strided like a fused qkv projection (Qwen3-8B: q 4096 +
+    k 1024 + v 1024 wide rows). Algorithmic bytes per token and layer: K and V
+    rows read and written (4 * H * D * 2) plus the 4-byte slot.
+    """
+    from kvoff import ops
+
+    device, caches = pool.device, pool  # the store overwrites random slots of the pool
+    tokens, q_width = 4096, 32 * w.head_dim
+    kv_width = w.heads * w.head_dim
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+    qkv = torch.randn((tokens, q_width + 2 * kv_width), generator=gen, device=device).to(
+        torch.bfloat16)
+    key = qkv[:, q_width:q_width + kv_width].view(tokens, w.heads, w.head_dim)
+    value = qkv[:, q_width + kv_width:].view(tokens, w.heads, w.head_dim)
+    num_slots = w.num_blocks * w.block_size
+    slots = torch.randperm(num_slots, generator=gen, device=device)[:tokens].to(torch.int32)
+    slots[::97] = -1  # padded positions are skipped
+    bad = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def ours():
+        for layer in range(w.layers):
+            ops.store_kvcache(key, value, caches[0, layer], caches[1, layer], slots)
+
+    valid = slots >= 0
+    idx = slots[valid].long()
+
+    def torch_scatter():  # the reference kernel's semantics as torch indexing
+        for layer in range(w.layers):
+            caches[0, layer].view(-1, kv_width)[idx] = key.reshape(tokens, -1)[valid]
+            caches[1, layer].view(-1, kv_width)[idx] = value.reshape(tokens, -1)[valid]
+
+    stream = torch.cuda.current_stream(device)
+    per_step = w.layers * tokens * (4 * kv_width * 2 + 4)
+    out = {"tokens": tokens, "layers": w.layers, "algorithmic_bytes_per_step": per_step}
+    for name, fn in (("kvoff", ours), ("torch_index_put", torch_scatter)):
+        ms = Timer(torch, stream, 1).run(fn, args.steps, args.warmup) / args.steps
+        out[name] = {"ms_per_step": ms, "GBps": per_step / (ms / 1e3) / 1e9,
+                     "us_per_launch": 1e3 * ms / w.layers}
+    out["kvoff"]["frac_of_hbm_peak"] = out["kvoff"]["GBps"] / hbm_peak
+    ops.store_kvcache(key, value, caches[0, 0], caches[1, 0], slots, bad_slots=bad)
+    torch.cuda.synchronize()
+    out["bad_slots"] = int(bad.item())
+    return out
 
 
 class _Block:
@@ -675,6 +725,10 @@ def run_ours(args) -> None:
     launches = (launches_per_call if save_mode == "mapped" else groups) + \
         (launches_per_call if restore_mode == "mapped" else groups)
 
+    # ---- prefill slot store (store_kvcache) ------------------------------------
+    store = store_kvcache_bench(torch, w, pool, args, hbm_peak) \
+        if not args.no_store else None
+
     # ---- through the drop-in CPUBlockCache: per-block calls vs batched calls ----
     dropin = dropin_e2e(torch, w, pool, save_ids, restore_ids, args, timer, main) \
         if w.batch <= 256 and not args.no_dropin else None
@@ -758,6 +812,7 @@ def run_ours(args) -> None:
         "pcie_memcpy_ceiling_GBps": ceiling,
         "sweep_GBps": sweep,
         "dropin_e2e_GBps": dropin,
+        "store_kvcache": store,
         "reference_gpu_path": ref_gpu,
     }
     if rank == 0:
