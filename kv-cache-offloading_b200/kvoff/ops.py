@@ -206,40 +206,70 @@ def memcpy(dst_ptr: int, src_ptr: int, nbytes: int, *, device, stream=None) -> N
         _lib.call("kvoff_memcpy", int(dst_ptr), int(src_ptr), int(nbytes), _stream(device, stream))
 
 
+_raw_current_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _fast_stream(device: torch.device, stream) -> int:
+    """Raw handle of `stream`, or of the device's current stream (cheap path)."""
+    if stream is None and _raw_current_stream is not None:
+        return _raw_current_stream(device.index)
+    return _stream(device, stream)
+
+
 def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
                   v_cache: torch.Tensor, slot_mapping: torch.Tensor, *,
                   bad_slots: torch.Tensor | None = None, stream=None) -> None:
     """Write row i of key/value [N, H, D] to cache slot slot_mapping[i] (-1: skip).
 
     Same contract as nanovllm/layers/attention.py:33-40 (including its layout
-    assertions); the scatter is one CUDA-graph-capturable kernel launch.
+    assertions); the scatter is one CUDA-graph-capturable kernel launch. This
+    runs once per layer per forward, so the host path is kept short: one
+    stride tuple per tensor, the raw current-stream handle, and a device
+    switch only when the tensors live on another device than the current one.
     """
     num_tokens, num_heads, head_dim = key.shape
     row = num_heads * head_dim
-    if not (key.stride(-1) == 1 and value.stride(-1) == 1):
+    ks, vs = key.stride(), value.stride()
+    if ks[2] != 1 or vs[2] != 1:
         raise AssertionError("key/value last dim must be contiguous")
-    if not (key.stride(1) == head_dim and value.stride(1) == head_dim):
+    if ks[1] != head_dim or vs[1] != head_dim:
         raise AssertionError("key/value heads must be dense")
-    if not (k_cache.stride(1) == row and v_cache.stride(1) == row):
+    if k_cache.stride(1) != row or v_cache.stride(1) != row:
         raise AssertionError("cache slots must hold dense [H, D] rows")
     if slot_mapping.numel() != num_tokens:
         raise AssertionError("one slot per token")
     if value.shape != key.shape:
         raise ValueError("key and value shapes differ")
-    if not (key.dtype == value.dtype == k_cache.dtype == v_cache.dtype):
+    dtype = key.dtype
+    if value.dtype != dtype or k_cache.dtype != dtype or v_cache.dtype != dtype:
         raise ValueError("key, value and caches must share a dtype")
     if slot_mapping.dtype != torch.int32:
         raise ValueError("slot_mapping must be int32")
-    for t, what in ((key, "key"), (value, "value"), (k_cache, "k_cache"), (v_cache, "v_cache"),
-                    (slot_mapping, "slot_mapping")):
-        _require_cuda(t, what)
+    if not (key.is_cuda and value.is_cuda and k_cache.is_cuda and v_cache.is_cuda
+            and slot_mapping.is_cuda):
+        raise ValueError("key, value, caches and slot_mapping must be CUDA tensors")
     if bad_slots is not None and (bad_slots.dtype != torch.int32 or not bad_slots.is_cuda):
         raise ValueError("bad_slots must be a CUDA int32 tensor")
     e = key.element_size()
     num_slots = k_cache.numel() // row if row else 0
-    with torch.cuda.device(key.device):
-        _lib.call("kvoff_store_kvcache", key.data_ptr(), key.stride(0) * e, value.data_ptr(),
-                  value.stride(0) * e, k_cache.data_ptr(), v_cache.data_ptr(), row * e,
-                  slot_mapping.data_ptr(), num_tokens, num_slots,
-                  bad_slots.data_ptr() if bad_slots is not None else None,
-                  _stream(key.device, stream))
+    device = key.device
+    args = (key.data_ptr(), ks[0] * e, value.data_ptr(), vs[0] * e, k_cache.data_ptr(),
+            v_cache.data_ptr(), row * e, slot_mapping.data_ptr(), num_tokens, num_slots,
+            bad_slots.data_ptr() if bad_slots is not None else None)
+    if device.index == torch.cuda.current_device():
+        status = _store_fn()(*args, _fast_stream(device, stream))
+    else:
+        with torch.cuda.device(device):
+            status = _store_fn()(*args, _fast_stream(device, stream))
+    if status:
+        _lib.check(status, "kvoff_store_kvcache")
+
+
+_STORE = None
+
+
+def _store_fn():
+    global _STORE
+    if _STORE is None:
+        _STORE = _lib.lib().kvoff_store_kvcache
+    return _STORE
