@@ -371,8 +371,9 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
     """Prefill slot store (BASELINE config 5 shape): 4096 new tokens per step for
     each of the model's layers, scattered into non-contiguous free slots of the
     pool, from K/V views strided like a fused qkv projection (Qwen3-8B: q 4096 +
-    k 1024 + v 1024 wide rows). Algorithmic bytes per token and layer: K and V
-    rows read and written (4 * H * D * 2) plus the 4-byte slot.
+    k 1024 + v 1024 wide rows, a separate projection output per layer).
+    Algorithmic bytes per token and layer: K and V rows read and written
+    (4 * H * D * 2) plus the 4-byte slot.
     """
     from kvoff import ops
 
@@ -381,10 +382,13 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
     kv_width = w.heads * w.head_dim
     gen = torch.Generator(device=device)
     gen.manual_seed(7)
-    qkv = torch.randn((tokens, q_width + 2 * kv_width), generator=gen, device=device).to(
-        torch.bfloat16)
-    key = qkv[:, q_width:q_width + kv_width].view(tokens, w.heads, w.head_dim)
-    value = qkv[:, q_width + kv_width:].view(tokens, w.heads, w.head_dim)
+    # One qkv projection output per layer (1.8 GB in all), so sources come from HBM.
+    qkv = torch.randn((w.layers, tokens, q_width + 2 * kv_width), generator=gen,
+                      device=device).to(torch.bfloat16)
+    keys = [qkv[layer, :, q_width:q_width + kv_width].view(tokens, w.heads, w.head_dim)
+            for layer in range(w.layers)]
+    values = [qkv[layer, :, q_width + kv_width:].view(tokens, w.heads, w.head_dim)
+              for layer in range(w.layers)]
     num_slots = w.num_blocks * w.block_size
     slots = torch.randperm(num_slots, generator=gen, device=device)[:tokens].to(torch.int32)
     slots[::97] = -1  # padded positions are skipped
@@ -392,15 +396,16 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
 
     def ours():
         for layer in range(w.layers):
-            ops.store_kvcache(key, value, caches[0, layer], caches[1, layer], slots)
+            ops.store_kvcache(keys[layer], values[layer], caches[0, layer], caches[1, layer],
+                              slots)
 
     valid = slots >= 0
     idx = slots[valid].long()
 
     def torch_scatter():  # the reference kernel's semantics as torch indexing
         for layer in range(w.layers):
-            caches[0, layer].view(-1, kv_width)[idx] = key.reshape(tokens, -1)[valid]
-            caches[1, layer].view(-1, kv_width)[idx] = value.reshape(tokens, -1)[valid]
+            caches[0, layer].view(-1, kv_width)[idx] = keys[layer].reshape(tokens, -1)[valid]
+            caches[1, layer].view(-1, kv_width)[idx] = values[layer].reshape(tokens, -1)[valid]
 
     per_step = w.layers * tokens * (4 * kv_width * 2 + 4)
     out = {"tokens": tokens, "layers": w.layers, "algorithmic_bytes_per_step": per_step}
@@ -423,9 +428,10 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
                      "us_per_launch": 1e3 * ms / w.layers}
     out["kvoff_graph"]["frac_of_hbm_peak"] = out["kvoff_graph"]["GBps"] / hbm_peak
     del graph
-    ops.store_kvcache(key, value, caches[0, 0], caches[1, 0], slots, bad_slots=bad)
+    ops.store_kvcache(keys[0], values[0], caches[0, 0], caches[1, 0], slots, bad_slots=bad)
     torch.cuda.synchronize()
     out["bad_slots"] = int(bad.item())
+    del keys, values, qkv
     return out
 
 

@@ -4,10 +4,12 @@
 // Token i's K row (row_bytes, at key + i * key_stride_bytes) goes to
 // k_cache + slot * row_bytes, and likewise for V; slot = slot_mapping[i],
 // and -1 marks a padded token that is skipped. The copy is a pure byte move,
-// so any cache dtype is moved bit-exactly. A CTA of 128 threads owns one token
-// at a time: the slot index is loaded once per CTA iteration into a register
-// broadcast, and the K and V rows move with the widest unit (16, 8, 4, 2 or 1
-// bytes) that every address and stride allows. Offsets are 64-bit.
+// so any cache dtype is moved bit-exactly. CTAs of 128 threads stride over the
+// tokens; the K and V rows move with the widest unit (16, 8, 4, 2 or 1
+// bytes) that every address and stride allows. Offsets are 64-bit. A CTA
+// iteration covers kTokens tokens: their slots are loaded first, then every
+// thread issues all of its K and V loads before the stores, so each thread
+// keeps 2 * kTokens independent loads in flight.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -17,6 +19,7 @@ namespace kvoff {
 namespace {
 
 constexpr int kThreads = 128;
+constexpr int kTokens = 4;  // tokens per CTA iteration: 8 independent loads per thread
 
 template <typename V>
 __global__ void __launch_bounds__(kThreads)
@@ -26,22 +29,34 @@ __global__ void __launch_bounds__(kThreads)
                          int64_t row_bytes, const int32_t* __restrict__ slot_mapping,
                          int64_t num_tokens, int64_t num_slots, int32_t* bad_slots) {
   const int64_t vecs = row_bytes / (int64_t)sizeof(V);
-  for (int64_t i = blockIdx.x; i < num_tokens; i += gridDim.x) {
-    const int64_t slot = __ldg(slot_mapping + i);
-    if (slot < 0) continue;
-    if (slot >= num_slots) {
-      if (threadIdx.x == 0 && bad_slots != nullptr) atomicAdd(bad_slots, 1);
-      continue;
+  for (int64_t first = (int64_t)blockIdx.x * kTokens; first < num_tokens;
+       first += (int64_t)gridDim.x * kTokens) {
+    int64_t slot[kTokens];
+#pragma unroll
+    for (int t = 0; t < kTokens; ++t) {
+      const int64_t i = first + t;
+      slot[t] = i < num_tokens ? (int64_t)__ldg(slot_mapping + i) : -1;
+      if (slot[t] >= num_slots) {  // out of range: skipped, counted once per token
+        if (threadIdx.x == 0 && bad_slots != nullptr) atomicAdd(bad_slots, 1);
+        slot[t] = -1;
+      }
     }
-    const V* ks = reinterpret_cast<const V*>(key + i * key_stride);
-    const V* vs = reinterpret_cast<const V*>(value + i * value_stride);
-    V* kd = reinterpret_cast<V*>(k_cache + slot * row_bytes);
-    V* vd = reinterpret_cast<V*>(v_cache + slot * row_bytes);
     for (int64_t j = threadIdx.x; j < vecs; j += kThreads) {
-      const V k = __ldg(ks + j);
-      const V v = __ldg(vs + j);
-      kd[j] = k;
-      vd[j] = v;
+      V k[kTokens], v[kTokens];
+#pragma unroll
+      for (int t = 0; t < kTokens; ++t) {
+        if (slot[t] >= 0) {
+          k[t] = __ldg(reinterpret_cast<const V*>(key + (first + t) * key_stride) + j);
+          v[t] = __ldg(reinterpret_cast<const V*>(value + (first + t) * value_stride) + j);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < kTokens; ++t) {
+        if (slot[t] >= 0) {
+          reinterpret_cast<V*>(k_cache + slot[t] * row_bytes)[j] = k[t];
+          reinterpret_cast<V*>(v_cache + slot[t] * row_bytes)[j] = v[t];
+        }
+      }
     }
   }
 }
@@ -51,7 +66,7 @@ int launch(const void* key, int64_t ks, const void* value, int64_t vs, void* kc,
            int64_t row_bytes, const int32_t* slots, int64_t n, int64_t num_slots, int32_t* bad,
            cudaStream_t stream) {
   const void* kernel = (const void*)store_kvcache_kernel<V>;
-  const int64_t grid = grid_for(n, kernel, kThreads, 0, 0);
+  const int64_t grid = grid_for((n + kTokens - 1) / kTokens, kernel, kThreads, 0, 0);
   store_kvcache_kernel<V><<<grid, kThreads, 0, stream>>>(
       static_cast<const uint8_t*>(key), ks, static_cast<const uint8_t*>(value), vs,
       static_cast<uint8_t*>(kc), static_cast<uint8_t*>(vc), row_bytes, slots, n, num_slots, bad);
