@@ -69,6 +69,18 @@ class CPUCacheFullError(MemoryError):
     """The configured payload budget cannot admit another block."""
 
 
+class _FollowerManager:
+    """Layout-only stand-in for the block manager of a tensor-parallel follower
+    rank (its bookkeeping lives on rank 0)."""
+
+    def __init__(self, num_blocks: int, block_size: int):
+        self.blocks = range(num_blocks)
+        self.block_size = block_size
+        self.hash_to_block_id: dict[int, int] = {}
+        self._cpu_prefix_cache = None
+        self.admission_blocked = False
+
+
 # Copy methods for CUDA pools. FP8: "staged" (kernel into device staging,
 # DMA drain) or "mapped" (kernel reads/writes the pinned slot over PCIe).
 # BF16: "engine" (one strided DMA per block), "tma" (cp.async.bulk gather into
@@ -109,7 +121,9 @@ class CPUBlockCache:
                  hybrid: tuple[float, float, float] | None = None):
         if type(max_bytes) is not int or max_bytes <= 0:
             raise ValueError("max_bytes must be a positive integer")
-        if runner.world_size != 1:
+        tensor_parallel = runner.world_size != 1
+        if tensor_parallel and not callable(getattr(runner, "kvoff_tier", None)):
+            # Per-rank tiers need the engine's runner to forward kvoff_tier calls.
             raise NotImplementedError("CPU prefix blocks currently require TP=1")
         if not automatic and (save_on_release or prefetch or hybrid):
             raise ValueError("save_on_release, prefetch and hybrid require automatic=True")
@@ -124,23 +138,17 @@ class CPUBlockCache:
             raise ValueError("KV pool layout does not match the block manager")
         if pool.device.type not in ("cpu", "cuda"):
             raise ValueError("KV pool must be on CPU or CUDA")
-        self._cache = pool
+        if tensor_parallel and pool.device.type != "cuda":
+            raise ValueError("a tensor-parallel CPU tier needs CUDA KV pools")
         self._manager = block_manager
-        self._fp8 = fp8
-        self._shape = (2, pool.shape[1], *pool.shape[3:])
-        self._scale_shape = (*self._shape[:-1], 1)
-        self._dtype = torch.float8_e4m3fn if fp8 else pool.dtype
-        self._payload_bytes = prod(self._shape) * self._dtype.itemsize
-        self._scale_bytes = prod(self._scale_shape) * pool.element_size() if fp8 else 0
-        self._block_bytes = self._payload_bytes + self._scale_bytes
+        self._setup_storage(pool, fp8, split_streams)
+        # Under tensor parallelism every rank stores its own KV heads of each
+        # block; the budget counts the block's payload over all ranks.
+        self._tp_runner = runner if tensor_parallel else None
+        self._block_bytes = self._slot_bytes * runner.world_size
         self._max_bytes = max_bytes
         self._capacity = max_bytes // self._block_bytes
         self._entries: dict[int, _CPUBlock] = {}
-        self._slabs: list[torch.Tensor] = []
-        self._scale_slabs: list[torch.Tensor] = []
-        self._slab_owners: list = []  # PinnedSlab per chunk (CUDA pools)
-        self._free_slots: list[int] = []
-        self._num_slots = 0
         self._hybrid = hybrid
         self._save_on_release = save_on_release
         self._prefetch = prefetch
@@ -148,9 +156,35 @@ class CPUBlockCache:
         self._saved_blocks = 0
         self._restored_blocks = 0
         self._budget_skips = 0
+        if tensor_parallel:
+            self._rpc("init", fp8, split_streams)
+        if automatic:
+            if block_manager._cpu_prefix_cache is not None:
+                raise RuntimeError("block manager already has an automatic CPU cache")
+            block_manager._cpu_prefix_cache = self
+        if preallocate:
+            while self._num_slots < self._capacity:
+                self._grow()
+
+    def _setup_storage(self, pool: torch.Tensor, fp8: bool, split_streams: bool):
+        """Slot layout, slabs, copy streams and ordering events for `pool`."""
+        self._cache = pool
+        self._fp8 = fp8
+        self._shape = (2, pool.shape[1], *pool.shape[3:])
+        self._scale_shape = (*self._shape[:-1], 1)
+        self._dtype = torch.float8_e4m3fn if fp8 else pool.dtype
+        self._payload_bytes = prod(self._shape) * self._dtype.itemsize
+        self._scale_bytes = prod(self._scale_shape) * pool.element_size() if fp8 else 0
+        self._slot_bytes = self._payload_bytes + self._scale_bytes
+        self._slabs: list[torch.Tensor] = []
+        self._scale_slabs: list[torch.Tensor] = []
+        self._slab_owners: list = []  # PinnedSlab per chunk (CUDA pools)
+        self._free_slots: list[int] = []
+        self._num_slots = 0
         self._on_cuda = pool.device.type == "cuda"
         self._copy_stream = self._restore_stream = None
         self._slot_reads: dict[int, torch.cuda.Event] = {}  # slot -> last restore reading it
+        self._slot_saved: dict[int, torch.cuda.Event] = {}  # slot -> its save (TP followers)
         self._pending_saves: dict[int, torch.cuda.Event] = {}  # GPU block -> save done
         self._pending_restores: dict[int, torch.cuda.Event] = {}  # GPU block -> restore done
         self._staging: dict = {}
@@ -168,13 +202,59 @@ class CPUBlockCache:
             self._copy_stream = torch.cuda.Stream(pool.device)
             self._restore_stream = (torch.cuda.Stream(pool.device) if split_streams
                                     else self._copy_stream)
-        if automatic:
-            if block_manager._cpu_prefix_cache is not None:
-                raise RuntimeError("block manager already has an automatic CPU cache")
-            block_manager._cpu_prefix_cache = self
-        if preallocate:
-            while self._num_slots < self._capacity:
-                self._grow()
+
+    # -- tensor parallelism ----------------------------------------------------
+    #
+    # Rank 0's cache (the leader) keeps all bookkeeping and copies its own KV
+    # heads; every device operation is mirrored to the other ranks through the
+    # engine's runner RPC (runner.call("kvoff_tier", op, ...), see
+    # kvoff.tp_tier), where a follower cache performs the same ordered copies on
+    # that rank's shard of the pool, into the same slot numbers.
+
+    @classmethod
+    def _follower(cls, runner, fp8: bool, split_streams: bool) -> "CPUBlockCache":
+        self = cls.__new__(cls)
+        pool = runner.kv_cache
+        self._manager = _FollowerManager(pool.shape[2], pool.shape[3])
+        self._setup_storage(pool, fp8, split_streams)
+        self._tp_runner = None
+        self._block_bytes = self._slot_bytes
+        self._max_bytes = self._capacity = 1 << 62  # slots are chosen by the leader
+        self._entries = {}
+        self._hybrid = None
+        self._save_on_release = self._prefetch = False
+        self._prefetched_blocks = self._saved_blocks = self._restored_blocks = 0
+        self._budget_skips = 0
+        return self
+
+    def _rpc(self, op: str, *args):
+        if self._tp_runner is not None:
+            from kvoff.tp_tier import send
+
+            send(self._tp_runner, op, *args)
+
+    def _tp_grow(self, count: int):
+        self._grow(count)
+
+    def _tp_save(self, block_ids, slots):
+        done = self._save_on_device(block_ids, slots)
+        for slot in slots:
+            self._slot_saved[slot] = done
+
+    def _tp_restore(self, slots, block_ids, wait: bool):
+        entries = [_CPUBlock((), None, slot, None, self._slot_saved.get(slot)) for slot in slots]
+        self._copy_entries(entries, block_ids, wait)
+
+    def _tp_before_reuse(self, block_ids):
+        for block_id in block_ids:
+            self.before_block_reuse(block_id)
+
+    def _tp_before_use(self, block_ids):
+        for block_id in block_ids:
+            self.before_block_use(block_id)
+
+    def _tp_synchronize(self):
+        self.synchronize()
 
     # -- properties ---------------------------------------------------------
 
@@ -246,10 +326,12 @@ class CPUBlockCache:
 
     # -- slots ----------------------------------------------------------------
 
-    def _grow(self):
+    def _grow(self, count: int | None = None):
         """Add one slab chunk of slots (pinned and NUMA-local for CUDA pools)."""
-        count = min(max(1, _SLAB_CHUNK_BYTES // self._block_bytes),
-                    self._capacity - self._num_slots)
+        if count is None:
+            count = min(max(1, _SLAB_CHUNK_BYTES // self._block_bytes),
+                        self._capacity - self._num_slots)
+            self._rpc("grow", count)
         if self._on_cuda:
             from kvoff.slab import PinnedSlab
 
@@ -447,6 +529,7 @@ class CPUBlockCache:
         """Wait for every pending host<->device copy (needed before host reads)."""
         for stream in {self._copy_stream, self._restore_stream} - {None}:
             stream.synchronize()
+        self._rpc("synchronize")
 
     @torch.inference_mode()
     def save_block(self, prefix_hash: int) -> bool:
@@ -563,6 +646,7 @@ class CPUBlockCache:
             done.record(copy)
         for block_id in block_ids:
             self._pending_saves[block_id] = done
+        self._rpc("save", list(block_ids), list(slots))
         return done
 
     def _preserve(self, prefix_hash: int):
@@ -585,16 +669,21 @@ class CPUBlockCache:
 
     def before_block_reuse(self, block_id: int):
         """Order later writes of a GPU block after its pending copies (no host sync)."""
+        waited = False
         for pending in (self._pending_saves, self._pending_restores):
             done = pending.pop(block_id, None)
             if done is not None:
                 torch.cuda.current_stream(self._cache.device).wait_event(done)
+                waited = True
+        if waited:  # the other ranks hold the same pending copies
+            self._rpc("before_reuse", [block_id])
 
     def before_block_use(self, block_id: int):
         """Order later reads of a prefetched GPU block after its restore."""
         done = self._pending_restores.pop(block_id, None)
         if done is not None:
             torch.cuda.current_stream(self._cache.device).wait_event(done)
+            self._rpc("before_use", [block_id])
 
     def _entry_for(self, prefix_hash: int, token_ids):
         """Pure lookup for admission planning; entries stay valid during copies."""
@@ -627,6 +716,7 @@ class CPUBlockCache:
             current.wait_event(done)
         else:
             self._pending_restores[block_id] = done
+        self._rpc("restore", [entry.slot], [block_id], wait)
         self._restored_blocks += 1
 
     @torch.inference_mode()
@@ -669,6 +759,7 @@ class CPUBlockCache:
         else:
             for block_id in block_ids:
                 self._pending_restores[block_id] = done
+        self._rpc("restore", [e.slot for e in entries], block_ids, wait)
         self._restored_blocks += len(entries)
 
     @torch.inference_mode()
@@ -705,9 +796,11 @@ class CPUBlockCache:
         if self.automatic:
             self._manager._cpu_prefix_cache = None
         self.synchronize()
+        self._rpc("close")
+        self._tp_runner = None
         self.clear()
         for table in (self._pending_saves, self._pending_restores, self._slot_reads,
-                      self._staging):
+                      self._slot_saved, self._staging):
             table.clear()
         self._slabs.clear()
         self._scale_slabs.clear()
