@@ -528,7 +528,10 @@ def run_ours(args) -> None:
     save_stream = torch.cuda.Stream(device)
     restore_stream = torch.cuda.Stream(device)
     timer = Timer(torch, main, world)
-    sweep_batches = [b for b in SWEEP_BATCHES if b <= B] if not args.no_sweep else []
+    # Per-GPU characterizations (mode sweep, drop-in cache, slot store, torch-op
+    # comparison) run at N=1; multi-GPU runs time only the contract's steps.
+    single = world == 1
+    sweep_batches = [b for b in SWEEP_BATCHES if b <= B] if single and not args.no_sweep else []
     bf16_batch = max(sweep_batches, default=0)
 
     pool = torch.empty((2, w.layers, w.num_blocks, w.block_size, w.heads, w.head_dim),
@@ -746,11 +749,11 @@ def run_ours(args) -> None:
 
     # ---- prefill slot store (store_kvcache) ------------------------------------
     store = store_kvcache_bench(torch, w, pool, args, hbm_peak) \
-        if not args.no_store else None
+        if single and not args.no_store else None
 
     # ---- through the drop-in CPUBlockCache: per-block calls vs batched calls ----
     dropin = dropin_e2e(torch, w, pool, save_ids, restore_ids, args, timer, main) \
-        if w.batch <= 256 and not args.no_dropin else None
+        if single and w.batch <= 256 and not args.no_dropin else None
 
     # ---- PCIe ceiling: pinned memcpy per direction and duplex -------------------
     blocks = min(B, 64, max(1, int(2.5e9 // w.fp8_block)))
@@ -780,7 +783,10 @@ def run_ours(args) -> None:
     pcie_per_dir = B * w.fp8_block / (e2e_ms / 1e3) / 1e9
 
     # ---- the reference's device path (torch ops) for context ------------------
+    ref_gpu = None
     try:
+        if not single:
+            raise StopIteration  # measured at N=1 only
         from kvoff.cpu_prefix_cache import fp8_dequantize, fp8_quantize
 
         shape = (2, w.layers, w.block_size, w.heads, w.head_dim)
@@ -795,6 +801,8 @@ def run_ours(args) -> None:
         ms = Timer(torch, main, 1).run(aten_step, 3, 3) / 3
         ref_gpu = {"what": "reference fp8_quantize + fp8_dequantize as torch ops on this GPU",
                    "GBps": 2 * len(few_ids) * w.bf16_block / (ms / 1e3) / 1e9}
+    except StopIteration:
+        pass
     except Exception as exc:  # context only; never fails the bench
         ref_gpu = {"error": str(exc)[:200]}
 
