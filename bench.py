@@ -473,8 +473,9 @@ def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, mai
     cache.synchronize()
 
     def join():
-        main.wait_stream(cache._copy_stream)
-        main.wait_stream(cache._restore_stream)
+        for b in restore_ids:  # the engine's first use of each restored block
+            cache.before_block_use(b)
+        main.wait_stream(cache._copy_stream)  # the drains to host
         for h in saves:
             cache.discard(h)
 
@@ -493,6 +494,30 @@ def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, mai
     for name, step in (("per_block", per_block), ("batched", batched)):
         ms = timer.run(step, args.steps, args.warmup) / args.steps
         out[name] = 2 * B * w.bf16_block / (ms / 1e3) / 1e9
+    # How long the compute stream waits before it may rewrite a block it just
+    # saved (save_block, then before_block_reuse), against the wait for the
+    # whole drain to host (the saved entry's event). Device time on the compute
+    # stream; a sleep ahead of it keeps host enqueue time out of the interval.
+    waits = {"reuse_wait_ms": [], "drain_ms": []}
+    for i, h in enumerate(saves[:16] * 2):
+        for name in waits:
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            main.synchronize()
+            torch.cuda._sleep(4_000_000)  # about 2 ms, longer than the host calls below
+            start.record(main)
+            cache.save_block(h)
+            if name == "reuse_wait_ms":
+                cache.before_block_reuse(manager.hash_to_block_id[h])
+            else:
+                main.wait_event(cache._entries[h].saved)
+            end.record(main)
+            end.synchronize()
+            if i >= 16:  # the first pass warms up
+                waits[name].append(start.elapsed_time(end))
+            cache.synchronize()
+            cache.discard(h)
+    out.update({name: statistics.median(v) for name, v in waits.items()})
     # The hybrid planner's restore cost at the batch sizes admission restores.
     out["restore_ms_per_block"] = {
         str(b): 1e3 * cache.measure_restore_s_per_block(repeats=max(1, 64 // b), batch=b)

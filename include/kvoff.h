@@ -128,6 +128,27 @@ KVOFF_API int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks,
                                            void* stream);
 
 /*
+ * kvoff_fp8_save_blocks_staged with explicit ordering. When num_wait_events > 0
+ * the quantize kernels wait for those events (cudaEvent_t handles, e.g. the
+ * point where the pool blocks were last written) instead of for all earlier
+ * work on `stream`, so they can overlap the DMA of earlier calls; the caller
+ * then orders the host-slot writes on `stream` itself. source_done, when not
+ * NULL, is recorded once every pool block of the call has been read: a block
+ * may be overwritten after it, before the slow drain to host finishes. Used by
+ * CPUBlockCache.save_block (cpu_prefix_cache.py:306-322) and
+ * before_block_reuse (:352-357).
+ */
+KVOFF_API int kvoff_fp8_save_blocks_staged_ev(const void* pool, int64_t num_chunks,
+                                              int64_t chunk_stride, int64_t block_stride,
+                                              int64_t num_blocks, int64_t rows_per_chunk,
+                                              int64_t head_dim, const int64_t* block_ids,
+                                              int64_t count, void* const* host_payload,
+                                              void* const* host_scale, void* staging_payload,
+                                              void* staging_scale, int64_t staging_blocks,
+                                              void* const* wait_events, int32_t num_wait_events,
+                                              void* source_done, void* stream);
+
+/*
  * Staged FP8 save that allocates nothing, for callers that cannot allocate
  * device memory while saving: an engine that gives nearly all free HBM to its
  * KV pool at start-up has no room left for a staging buffer, and a host
@@ -164,6 +185,31 @@ KVOFF_API int kvoff_fp8_restore_blocks_staged(void* pool, int64_t num_chunks,
                                               const void* const* host_scale,
                                               void* staging_payload, void* staging_scale,
                                               int64_t staging_blocks, void* stream);
+
+/*
+ * kvoff_fp8_restore_blocks_staged that signals completion on `done_event`
+ * (recorded after the last pool write) instead of making `stream` wait for
+ * the dequantize kernels, so the next call's host-to-device copies can start
+ * while this call's kernels run. The caller orders readers of the blocks on
+ * done_event; kvoff_stream_join_pipeline(stream) makes `stream` itself wait.
+ * Used by CPUBlockCache._copy_entry (cpu_prefix_cache.py:371-393).
+ */
+KVOFF_API int kvoff_fp8_restore_blocks_staged_ev(void* pool, int64_t num_chunks,
+                                                 int64_t chunk_stride, int64_t block_stride,
+                                                 int64_t num_blocks, int64_t rows_per_chunk,
+                                                 int64_t head_dim, const int64_t* block_ids,
+                                                 int64_t count, const void* const* host_payload,
+                                                 const void* const* host_scale,
+                                                 void* staging_payload, void* staging_scale,
+                                                 int64_t staging_blocks, void* done_event,
+                                                 void* stream);
+
+/*
+ * Make `stream` wait for all work the staged calls queued on their internal
+ * kernel stream for `stream` (needed before synchronizing `stream` or freeing
+ * its staging buffers after *_ev calls). No-op when there is none.
+ */
+KVOFF_API int kvoff_stream_join_pipeline(void* stream);
 
 /*
  * Byte-exact block passthrough (BF16 mode): move whole blocks between the

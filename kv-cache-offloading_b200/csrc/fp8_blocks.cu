@@ -507,15 +507,18 @@ int kvoff_fp8_restore_blocks(void* pool, int64_t num_chunks, int64_t chunk_strid
   return ok();
 }
 
-int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks, int64_t chunk_stride,
-                                 int64_t block_stride, int64_t num_blocks,
-                                 int64_t rows_per_chunk, int64_t head_dim,
-                                 const int64_t* block_ids, int64_t count,
-                                 void* const* host_payload, void* const* host_scale,
-                                 void* staging_payload, void* staging_scale,
-                                 int64_t staging_blocks, void* stream) {
+int kvoff_fp8_save_blocks_staged_ev(const void* pool, int64_t num_chunks, int64_t chunk_stride,
+                                    int64_t block_stride, int64_t num_blocks,
+                                    int64_t rows_per_chunk, int64_t head_dim,
+                                    const int64_t* block_ids, int64_t count,
+                                    void* const* host_payload, void* const* host_scale,
+                                    void* staging_payload, void* staging_scale,
+                                    int64_t staging_blocks, void* const* wait_events,
+                                    int32_t num_wait_events, void* source_done, void* stream) {
   if (injected("fp8_save_blocks_staged")) return KVOFF_EINJECTED;
   Args a{"fp8_save_blocks_staged", const_cast<void*>(pool), {}, num_blocks, block_ids, count};
+  if (num_wait_events < 0 || (num_wait_events > 0 && wait_events == nullptr))
+    return fail(KVOFF_EINVAL, "kvoff_fp8_save_blocks_staged_ev: bad wait event list");
   KVOFF_TRY(validate(a, num_chunks, chunk_stride, block_stride, rows_per_chunk, head_dim));
   if (count == 0) return ok();
   if (host_payload == nullptr || host_scale == nullptr || staging_payload == nullptr ||
@@ -538,6 +541,12 @@ int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks, int64_t c
     lock.lock();
     KVOFF_TRY(pipe_for(s, staging_payload, &p));
     ks = p->aux;
+  }
+  if (num_wait_events > 0) {  // the kernels need only these, not earlier DMA on `s`
+    for (int32_t i = 0; i < num_wait_events; ++i)
+      KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, static_cast<cudaEvent_t>(wait_events[i]), 0),
+                            "cudaStreamWaitEvent (wait event)"));
+  } else if (pipelined) {
     KVOFF_TRY(cuda_status(cudaEventRecord(p->start, s), "cudaEventRecord"));
     KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, p->start, 0), "cudaStreamWaitEvent"));
   }
@@ -556,6 +565,9 @@ int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks, int64_t c
     sub.block_ids = block_ids + first;
     sub.count = n;
     KVOFF_TRY(launch<true>(sub, pdst, sdst, 0, ks));
+    if (source_done != nullptr && first + n >= count)  // every pool block has been read
+      KVOFF_TRY(cuda_status(cudaEventRecord(static_cast<cudaEvent_t>(source_done), ks),
+                            "cudaEventRecord (source done)"));
     if (pipelined) {
       KVOFF_TRY(cuda_status(cudaEventRecord(p->ready[h], ks), "cudaEventRecord"));
       KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p->ready[h], 0), "cudaStreamWaitEvent"));
@@ -571,13 +583,14 @@ int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks, int64_t c
   return ok();
 }
 
-int kvoff_fp8_restore_blocks_staged(void* pool, int64_t num_chunks, int64_t chunk_stride,
-                                    int64_t block_stride, int64_t num_blocks,
-                                    int64_t rows_per_chunk, int64_t head_dim,
-                                    const int64_t* block_ids, int64_t count,
-                                    const void* const* host_payload,
-                                    const void* const* host_scale, void* staging_payload,
-                                    void* staging_scale, int64_t staging_blocks, void* stream) {
+int kvoff_fp8_restore_blocks_staged_ev(void* pool, int64_t num_chunks, int64_t chunk_stride,
+                                       int64_t block_stride, int64_t num_blocks,
+                                       int64_t rows_per_chunk, int64_t head_dim,
+                                       const int64_t* block_ids, int64_t count,
+                                       const void* const* host_payload,
+                                       const void* const* host_scale, void* staging_payload,
+                                       void* staging_scale, int64_t staging_blocks,
+                                       void* done_event, void* stream) {
   if (injected("fp8_restore_blocks_staged")) return KVOFF_EINJECTED;
   Args a{"fp8_restore_blocks_staged", pool, {}, num_blocks, block_ids, count};
   KVOFF_TRY(validate(a, num_chunks, chunk_stride, block_stride, rows_per_chunk, head_dim));
@@ -635,10 +648,52 @@ int kvoff_fp8_restore_blocks_staged(void* pool, int64_t num_chunks, int64_t chun
       p->next = 1 - h;
     }
   }
-  if (pipelined) {  // the caller's stream sees every pool write of this call
+  if (done_event != nullptr) {  // the caller orders later work on this event instead
+    KVOFF_TRY(cuda_status(cudaEventRecord(static_cast<cudaEvent_t>(done_event), ks),
+                          "cudaEventRecord (done)"));
+  } else if (pipelined) {  // the caller's stream sees every pool write of this call
     KVOFF_TRY(cuda_status(cudaEventRecord(p->done, ks), "cudaEventRecord"));
     KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p->done, 0), "cudaStreamWaitEvent"));
   }
+  return ok();
+}
+
+int kvoff_fp8_save_blocks_staged(const void* pool, int64_t num_chunks, int64_t chunk_stride,
+                                 int64_t block_stride, int64_t num_blocks,
+                                 int64_t rows_per_chunk, int64_t head_dim,
+                                 const int64_t* block_ids, int64_t count,
+                                 void* const* host_payload, void* const* host_scale,
+                                 void* staging_payload, void* staging_scale,
+                                 int64_t staging_blocks, void* stream) {
+  return kvoff_fp8_save_blocks_staged_ev(pool, num_chunks, chunk_stride, block_stride, num_blocks,
+                                         rows_per_chunk, head_dim, block_ids, count, host_payload,
+                                         host_scale, staging_payload, staging_scale,
+                                         staging_blocks, nullptr, 0, nullptr, stream);
+}
+
+int kvoff_fp8_restore_blocks_staged(void* pool, int64_t num_chunks, int64_t chunk_stride,
+                                    int64_t block_stride, int64_t num_blocks,
+                                    int64_t rows_per_chunk, int64_t head_dim,
+                                    const int64_t* block_ids, int64_t count,
+                                    const void* const* host_payload,
+                                    const void* const* host_scale, void* staging_payload,
+                                    void* staging_scale, int64_t staging_blocks, void* stream) {
+  return kvoff_fp8_restore_blocks_staged_ev(pool, num_chunks, chunk_stride, block_stride,
+                                            num_blocks, rows_per_chunk, head_dim, block_ids,
+                                            count, host_payload, host_scale, staging_payload,
+                                            staging_scale, staging_blocks, nullptr, stream);
+}
+
+int kvoff_stream_join_pipeline(void* stream) {
+  int dev = 0;
+  KVOFF_TRY(cuda_status(cudaGetDevice(&dev), "cudaGetDevice"));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::lock_guard<std::mutex> lock(g_pipe_mu);
+  auto it = g_pipes.find({dev, s});
+  if (it == g_pipes.end()) return ok();
+  Pipe& p = it->second;
+  KVOFF_TRY(cuda_status(cudaEventRecord(p.done, p.aux), "cudaEventRecord"));
+  KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p.done, 0), "cudaStreamWaitEvent"));
   return ok();
 }
 

@@ -40,6 +40,13 @@ SIGNATURES = {
                                                             _I64, _PI64, _I64, _PP, _PP, _P]),
     "kvoff_fp8_restore_blocks_staged": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _I64,
                                                        _PI64, _I64, _PP, _PP, _P, _P, _I64, _P]),
+    "kvoff_fp8_save_blocks_staged_ev": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _I64,
+                                                       _PI64, _I64, _PP, _PP, _P, _P, _I64, _PP,
+                                                       _I32, _P, _P]),
+    "kvoff_fp8_restore_blocks_staged_ev": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _I64,
+                                                          _PI64, _I64, _PP, _PP, _P, _P, _I64, _P,
+                                                          _P]),
+    "kvoff_stream_join_pipeline": (ctypes.c_int, [_P]),
     "kvoff_copy_blocks": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _PI64, _I64, _PP, _I32,
                                          _I32, _I32, _P]),
     "kvoff_copy_tokens": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _PI64, _I64, _P,

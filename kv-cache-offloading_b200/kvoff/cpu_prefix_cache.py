@@ -378,6 +378,8 @@ class CPUBlockCache:
         staged = self._staging.get(stream)
         if staged is None or staged[0].shape[0] < want:
             device = self._cache.device
+            if staged is not None:  # kernels of earlier calls may still use it
+                self._ops.join_pipeline(device, stream)
             scales = (torch.empty((want, self._scale_bytes), dtype=torch.uint8, device=device)
                       if self._fp8 else None)
             staged = (torch.empty((want, self._payload_bytes), dtype=torch.uint8, device=device),
@@ -401,8 +403,12 @@ class CPUBlockCache:
         pairs = [self._slot_pointers(slot, mapped) for slot in slots]
         return [p for p, _ in pairs], [s for _, s in pairs]
 
-    def _device_save(self, pool: torch.Tensor, block_ids, slots, stream):
-        """Enqueue pool blocks -> slots on `stream` (one native call per method)."""
+    def _device_save(self, pool: torch.Tensor, block_ids, slots, stream, wait_events=None,
+                     source_done=None):
+        """Enqueue pool blocks -> slots on `stream` (one native call per method).
+
+        wait_events / source_done apply to staged FP8 saves (ops.save_fp8_staged).
+        """
         ops, modes = self._ops, self._modes
         if self._fp8:
             mapped = modes["fp8_save"] == "mapped"
@@ -411,7 +417,8 @@ class CPUBlockCache:
                 ops.save_fp8(pool, block_ids, payload, scale, stream=stream)
             else:
                 ops.save_fp8_staged(pool, block_ids, payload, scale,
-                                    *self._stage(stream, len(block_ids)), stream=stream)
+                                    *self._stage(stream, len(block_ids)), stream=stream,
+                                    wait_events=wait_events, source_done=source_done)
             return
         method = modes["bf16_save"]
         payload, _ = self._pointers(slots, method == "sm")
@@ -428,16 +435,19 @@ class CPUBlockCache:
             ops.copy_blocks(pool, block_ids, payload, stream=stream,
                             method=ops.COPY_SM if method == "sm" else ops.COPY_ENGINE)
 
-    def _device_restore(self, pool: torch.Tensor, block_ids, plain, mapped, stream):
+    def _device_restore(self, pool: torch.Tensor, block_ids, plain, mapped, stream,
+                        done_event=None):
         """Enqueue slots -> pool blocks on `stream`; plain / mapped are the slots'
-        (payload, scale) host pointers and device aliases."""
+        (payload, scale) host pointers and device aliases. done_event applies to
+        staged FP8 restores (ops.restore_fp8_staged)."""
         ops, modes = self._ops, self._modes
         if self._fp8:
             if modes["fp8_restore"] == "mapped":
                 ops.restore_fp8(pool, block_ids, *mapped, stream=stream)
             else:
                 ops.restore_fp8_staged(pool, block_ids, *plain,
-                                       *self._stage(stream, len(block_ids)), stream=stream)
+                                       *self._stage(stream, len(block_ids)), stream=stream,
+                                       done_event=done_event)
             return
         method = modes["bf16_restore"]
         if method == "tma":
@@ -455,9 +465,23 @@ class CPUBlockCache:
         else:
             ops.copy_blocks(pool, block_ids, plain[0], restore=True, stream=stream)
 
-    def _restore_slots(self, slots, block_ids, stream):
+    def _restore_slots(self, slots, block_ids, stream) -> torch.cuda.Event:
+        """Restore slots into pool blocks on `stream`; returns the done event.
+
+        A staged FP8 restore records the event after its last dequantize kernel
+        (on the library's kernel stream), so `stream` is free to start the next
+        restore's copies while those kernels run; other methods record it on
+        `stream` after the copies.
+        """
+        done = torch.cuda.Event()
+        done.record(stream)  # creates the CUDA event; a staged restore re-records it
+        staged = self._fp8 and self._modes["fp8_restore"] == "staged"
         self._device_restore(self._cache, block_ids, self._pointers(slots, False),
-                             self._pointers(slots, True), stream)
+                             self._pointers(slots, True), stream,
+                             done_event=done if staged else None)
+        if not staged:
+            done.record(stream)
+        return done
 
     # -- host copies (CPU pools: the reference's synchronous path) ---------------
 
@@ -528,6 +552,7 @@ class CPUBlockCache:
     def synchronize(self):
         """Wait for every pending host<->device copy (needed before host reads)."""
         for stream in {self._copy_stream, self._restore_stream} - {None}:
+            self._ops.join_pipeline(self._cache.device, stream)
             stream.synchronize()
         self._rpc("synchronize")
 
@@ -629,23 +654,44 @@ class CPUBlockCache:
         return results
 
     def _save_on_device(self, block_ids, slots) -> torch.cuda.Event:
+        """Enqueue the save of pool blocks into slots; returns the slots-filled event.
+
+        The copies follow the kernels that wrote the blocks and, with split
+        streams, earlier restores that read these slots. before_block_reuse
+        orders each block's next writer after the point where the save has read
+        it: for staged FP8 that is the quantize kernel (the library records
+        `read` after it, while the copies to host still drain); otherwise the
+        returned event.
+        """
         pool = self._cache
         current = torch.cuda.current_stream(pool.device)
         copy = self._copy_stream
-        # After the kernels that wrote the blocks; with split streams also after
-        # earlier restores that read these slots. before_block_reuse orders each
-        # block's next writer after the returned event.
-        copy.wait_stream(current)
+        staged = self._fp8 and self._modes["fp8_save"] == "staged"
+        waits = read = None
+        if staged:
+            # The kernels wait only for the blocks' writers (and restores still
+            # filling them), not for earlier saves' copies on the copy stream.
+            ready = torch.cuda.Event()
+            ready.record(current)
+            waits = [ready]
+            for block_id in dict.fromkeys(block_ids):
+                restoring = self._pending_restores.get(block_id)
+                if restoring is not None:
+                    waits.append(restoring)
+            read = torch.cuda.Event()
+            read.record(copy)  # creates the CUDA event; the library re-records it
+        else:
+            copy.wait_stream(current)
         for slot in slots:
-            read = self._slot_reads.pop(slot, None)
-            if read is not None and self._restore_stream is not copy:
-                copy.wait_event(read)
+            slot_read = self._slot_reads.pop(slot, None)
+            if slot_read is not None and self._restore_stream is not copy:
+                copy.wait_event(slot_read)
         with torch.cuda.stream(copy):
-            self._device_save(pool, list(block_ids), list(slots), copy)
+            self._device_save(pool, list(block_ids), list(slots), copy, waits, read)
             done = torch.cuda.Event()
             done.record(copy)
         for block_id in block_ids:
-            self._pending_saves[block_id] = done
+            self._pending_saves[block_id] = read if read is not None else done
         self._rpc("save", list(block_ids), list(slots))
         return done
 
@@ -708,9 +754,7 @@ class CPUBlockCache:
         if entry.saved is not None and stream is not self._copy_stream:
             stream.wait_event(entry.saved)
         with torch.cuda.stream(stream):
-            self._restore_slots([entry.slot], [block_id], stream)
-            done = torch.cuda.Event()
-            done.record(stream)
+            done = self._restore_slots([entry.slot], [block_id], stream)
         self._slot_reads[entry.slot] = done
         if wait:
             current.wait_event(done)
@@ -749,9 +793,7 @@ class CPUBlockCache:
                     waited.add(id(entry.saved))
                     stream.wait_event(entry.saved)
         with torch.cuda.stream(stream):
-            self._restore_slots([e.slot for e in entries], block_ids, stream)
-            done = torch.cuda.Event()
-            done.record(stream)
+            done = self._restore_slots([e.slot for e in entries], block_ids, stream)
         for entry in entries:
             self._slot_reads[entry.slot] = done
         if wait:

@@ -128,10 +128,24 @@ def _staging_blocks(g: PoolGeometry, staging_payload: torch.Tensor,
     return count
 
 
+def _event(event) -> int:
+    """Raw cudaEvent_t of a recorded torch.cuda.Event (or a raw handle)."""
+    handle = int(getattr(event, "cuda_event", event))
+    if handle == 0:  # torch creates the CUDA event on its first record
+        raise ValueError("pass an event that has been recorded at least once")
+    return handle
+
+
 def save_fp8_staged(pool: torch.Tensor, block_ids, host_payload_ptrs, host_scale_ptrs,
                     staging_payload: torch.Tensor, staging_scale: torch.Tensor, *,
-                    stream=None) -> None:
-    """Quantize into device staging, then cudaMemcpyAsync each slot to pinned host."""
+                    stream=None, wait_events=None, source_done=None) -> None:
+    """Quantize into device staging, then cudaMemcpyAsync each slot to pinned host.
+
+    By default the quantize kernels follow all earlier work on `stream`. With
+    `wait_events` (recorded torch.cuda.Events) they follow only those, so they
+    can overlap the host copies of earlier calls; `source_done` is re-recorded
+    once the kernels have read every pool block of the call.
+    """
     _require_cuda(pool, "pool")
     _require_bf16(pool)
     g = geometry(pool)
@@ -139,18 +153,32 @@ def save_fp8_staged(pool: torch.Tensor, block_ids, host_payload_ptrs, host_scale
     if len(host_payload_ptrs) != n or len(host_scale_ptrs) != n:
         raise ValueError("one payload and scale pointer per block")
     staged = _staging_blocks(g, staging_payload, staging_scale)
+    common = (pool.data_ptr(), g.num_chunks, g.chunk_stride, g.block_stride, g.num_blocks,
+              g.rows_per_chunk, g.head_dim, _lib.int64_array(block_ids), n,
+              _lib.pointer_array(host_payload_ptrs), _lib.pointer_array(host_scale_ptrs),
+              staging_payload.data_ptr(), staging_scale.data_ptr(), staged)
     with torch.cuda.device(pool.device):
-        _lib.call("kvoff_fp8_save_blocks_staged", pool.data_ptr(), g.num_chunks, g.chunk_stride,
-                  g.block_stride, g.num_blocks, g.rows_per_chunk, g.head_dim,
-                  _lib.int64_array(block_ids), n, _lib.pointer_array(host_payload_ptrs),
-                  _lib.pointer_array(host_scale_ptrs), staging_payload.data_ptr(),
-                  staging_scale.data_ptr(), staged, _stream(pool.device, stream))
+        if wait_events is None and source_done is None:
+            _lib.call("kvoff_fp8_save_blocks_staged", *common, _stream(pool.device, stream))
+            return
+        waits = [_event(e) for e in (wait_events or ())]
+        _lib.call("kvoff_fp8_save_blocks_staged_ev", *common,
+                  _lib.pointer_array(waits) if waits else None, len(waits),
+                  _event(source_done) if source_done is not None else None,
+                  _stream(pool.device, stream))
 
 
 def restore_fp8_staged(pool: torch.Tensor, block_ids, host_payload_ptrs, host_scale_ptrs,
                        staging_payload: torch.Tensor, staging_scale: torch.Tensor, *,
-                       stream=None) -> None:
-    """cudaMemcpyAsync each pinned slot into device staging, then dequantize."""
+                       stream=None, done_event=None) -> None:
+    """cudaMemcpyAsync each pinned slot into device staging, then dequantize.
+
+    By default `stream` waits for the dequantize kernels before it returns to
+    the caller's later work. With `done_event` (a recorded torch.cuda.Event)
+    the event is re-recorded after the last pool write instead and `stream` is
+    left free to start the next call's copies; order readers on the event, or
+    call join_pipeline(stream) before synchronizing `stream`.
+    """
     _require_cuda(pool, "pool")
     _require_bf16(pool)
     g = geometry(pool)
@@ -158,12 +186,23 @@ def restore_fp8_staged(pool: torch.Tensor, block_ids, host_payload_ptrs, host_sc
     if len(host_payload_ptrs) != n or len(host_scale_ptrs) != n:
         raise ValueError("one payload and scale pointer per block")
     staged = _staging_blocks(g, staging_payload, staging_scale)
+    common = (pool.data_ptr(), g.num_chunks, g.chunk_stride, g.block_stride, g.num_blocks,
+              g.rows_per_chunk, g.head_dim, _lib.int64_array(block_ids), n,
+              _lib.pointer_array(host_payload_ptrs), _lib.pointer_array(host_scale_ptrs),
+              staging_payload.data_ptr(), staging_scale.data_ptr(), staged)
     with torch.cuda.device(pool.device):
-        _lib.call("kvoff_fp8_restore_blocks_staged", pool.data_ptr(), g.num_chunks,
-                  g.chunk_stride, g.block_stride, g.num_blocks, g.rows_per_chunk, g.head_dim,
-                  _lib.int64_array(block_ids), n, _lib.pointer_array(host_payload_ptrs),
-                  _lib.pointer_array(host_scale_ptrs), staging_payload.data_ptr(),
-                  staging_scale.data_ptr(), staged, _stream(pool.device, stream))
+        if done_event is None:
+            _lib.call("kvoff_fp8_restore_blocks_staged", *common, _stream(pool.device, stream))
+        else:
+            _lib.call("kvoff_fp8_restore_blocks_staged_ev", *common, _event(done_event),
+                      _stream(pool.device, stream))
+
+
+def join_pipeline(device, stream=None) -> None:
+    """Make `stream` wait for the staged calls' kernels queued on its behalf."""
+    device = torch.device(device)
+    with torch.cuda.device(device):
+        _lib.call("kvoff_stream_join_pipeline", _stream(device, stream))
 
 
 def copy_blocks(pool: torch.Tensor, block_ids, slot_ptrs, *, restore: bool = False,

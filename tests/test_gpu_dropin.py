@@ -186,6 +186,67 @@ def test_block_reuse_waits_for_pending_save(cuda):
     assert torch.equal(payload.view(torch.uint8).reshape(-1), expected.reshape(-1))
 
 
+def test_fp8_block_reuse_waits_for_the_read_not_the_drain(cuda):
+    """Staged FP8: before_block_reuse waits for the quantize kernel alone.
+
+    The copy stream sleeps before the save, so the drain to host is still
+    queued when the block is overwritten; the slot must still hold the block
+    as it was when saved.
+    """
+    engine = FakeEngine(finite_pool(SHAPES[1], cuda, seed=2))
+    m = engine.manager
+    key = m.publish(3)
+    source = bits_u16(engine.pool)
+    cache = engine.create_cpu_prefix_cache(per_block(engine.pool), fp8=True,
+                                           split_streams=True, preallocate=True)
+    assert cache._modes["fp8_save"] == "staged"
+    assert cache.save_block(key)  # allocates the staging buffers outside the timed part
+    cache.synchronize()
+    assert cache.discard(key)
+    with torch.cuda.stream(cache._copy_stream):
+        torch.cuda._sleep(5 * SLEEP_CYCLES)
+    assert cache.save_block(key)
+    cache.before_block_reuse(3)
+    engine.pool[:, :, 3].fill_(5)  # the block's next writer
+    torch.cuda.current_stream(cuda).synchronize()
+    assert not cache._copy_stream.query()  # the drain has not finished
+    cache.synchronize()
+    want_p, want_s = oracle.fp8_save_blocks(source, [3])
+    entry = cache._entries[key]
+    assert np.array_equal(entry.kv.view(torch.uint8).numpy(), want_p[0])
+    assert np.array_equal(bits_u16(entry.scale), want_s[0])
+
+
+def test_fp8_back_to_back_restores_match_oracle(cuda):
+    """Per-block staged restores share two staging halves without a join per
+    call; a batched restore on the same stream then grows the staging."""
+    shape = (2, 3, 16, 256, 8, 128)
+    engine = FakeEngine(finite_pool(shape, cuda, seed=6))
+    m = engine.manager
+    sources = [9, 2, 5, 7, 11, 0]
+    keys = [m.publish(b) for b in sources]
+    pool = engine.pool
+    source = bits_u16(pool)
+    cache = engine.create_cpu_prefix_cache(8 * per_block(pool), fp8=True, split_streams=True)
+    assert all(cache.save_block(k) for k in keys)
+    entries = [cache._entries[k] for k in keys]
+    want_p, want_s = oracle.fp8_save_blocks(source, sources)
+    expected = source.copy()
+    for rounds, targets in enumerate(([1, 3, 4, 6, 8, 10], [12, 13, 14, 15, 1, 3])):
+        if rounds == 0:
+            with torch.cuda.stream(cache._restore_stream):
+                torch.cuda._sleep(SLEEP_CYCLES)  # the copies queue up behind a slow start
+            for e, b in zip(entries, targets):
+                cache._copy_entry(e, b, wait=False)
+        else:
+            cache._copy_entries(entries, targets, wait=False)
+        for b in targets:
+            cache.before_block_use(b)
+        oracle.fp8_restore_blocks(expected, targets, want_p, want_s)
+        assert np.array_equal(bits_u16(pool), expected)
+    cache.synchronize()
+
+
 def test_injected_failures_roll_back_and_retry_is_byte_exact(cuda):
     engine = FakeEngine(arbitrary_pool(SHAPES[1], cuda))
     m = engine.manager
