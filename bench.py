@@ -47,7 +47,7 @@ METRIC = "KV restore+save GB/s (FP8, bf16-equivalent bytes)"
 # dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of the save
 # kernel on 8 config-2 blocks (profiles/fp8_save_kernel_config2.md), per byte of
 # bf16 block read; traffic scales with blocks because each is read and written once.
-SAVE_KERNEL_DRAM_BYTES_PER_BF16_BYTE = (302_010_880 + 103_050_240) / (8 * 37_748_736)
+SAVE_KERNEL_DRAM_BYTES_PER_BF16_BYTE = (302_021_632 + 100_535_552) / (8 * 37_748_736)
 
 
 @dataclass(frozen=True)

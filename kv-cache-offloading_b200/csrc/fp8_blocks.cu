@@ -5,7 +5,10 @@
 // Work decomposition: a "unit" is a tile of up to kTile consecutive rows of
 // one chunk (one K/V x layer slice) of one block. Rows of a tile are
 // contiguous in both the pool and the slot, so every warp instruction moves
-// contiguous bytes. A persistent grid strides over units.
+// contiguous bytes. The fast kernels launch one CTA per unit: on B200 an
+// oversubscribed grid of short CTAs keeps HBM busier than a persistent grid
+// striding over the units (restore 88 % -> 99 % of the measured copy peak,
+// save 95 % -> 100 %). The kernels still stride, so a max_ctas cap is valid.
 //
 // Save, fast path (D = 8 * LANES, LANES in {4, 8, 16, 32}): LANES lanes own
 // one row, each loading 16 bytes (8 bf16) with a non-coherent streaming load.
@@ -375,7 +378,7 @@ int launch(const Args& a, void* const* payload, void* const* scale, int32_t max_
     }
     if (lanes != 0) {
       const int64_t units = (int64_t)n * a.g.num_chunks * a.g.tiles_per_chunk;
-      const int64_t grid = grid_for(units, kernel, kThreads, 0, max_ctas);
+      const int64_t grid = (max_ctas > 0 && units > max_ctas) ? max_ctas : units;
       if (kSave) {
         switch (lanes) {
           case 2: fp8_save_kernel<2><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;
