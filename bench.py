@@ -369,15 +369,20 @@ def max_over_ranks(torch, value: float, device) -> float:
 
 def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict:
     """Prefill slot store (BASELINE config 5 shape): 4096 new tokens per step for
-    each of the model's layers, scattered into non-contiguous free slots of the
-    pool, from K/V views strided like a fused qkv projection (Qwen3-8B: q 4096 +
-    k 1024 + v 1024 wide rows, a separate projection output per layer).
+    each of the model's layers, from K/V views strided like a fused qkv
+    projection (Qwen3-8B: q 4096 + k 1024 + v 1024 wide rows, a separate
+    projection output per layer), into slots of the pool.
+
+    Two slot patterns: "block_slots" is what a prefill gets from the block
+    manager (16 random free blocks, 256 consecutive slots each); "random_slots"
+    scatters every token to an independent random slot (a stress case: each
+    2 KB row write opens its own DRAM page). Every 97th token is padding (-1).
     Algorithmic bytes per token and layer: K and V rows read and written
     (4 * H * D * 2) plus the 4-byte slot.
     """
     from kvoff import ops
 
-    device, caches = pool.device, pool  # the store overwrites random slots of the pool
+    device, caches = pool.device, pool  # the store overwrites slots of the pool
     tokens, q_width = 4096, 32 * w.head_dim
     kv_width = w.heads * w.head_dim
     gen = torch.Generator(device=device)
@@ -390,45 +395,55 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
     values = [qkv[layer, :, q_width + kv_width:].view(tokens, w.heads, w.head_dim)
               for layer in range(w.layers)]
     num_slots = w.num_blocks * w.block_size
-    slots = torch.randperm(num_slots, generator=gen, device=device)[:tokens].to(torch.int32)
-    slots[::97] = -1  # padded positions are skipped
-    bad = torch.zeros(1, dtype=torch.int32, device=device)
-
-    def ours():
-        for layer in range(w.layers):
-            ops.store_kvcache(keys[layer], values[layer], caches[0, layer], caches[1, layer],
-                              slots)
-
-    valid = slots >= 0
-    idx = slots[valid].long()
-
-    def torch_scatter():  # the reference kernel's semantics as torch indexing
-        for layer in range(w.layers):
-            caches[0, layer].view(-1, kv_width)[idx] = keys[layer].reshape(tokens, -1)[valid]
-            caches[1, layer].view(-1, kv_width)[idx] = values[layer].reshape(tokens, -1)[valid]
-
+    blocks = torch.randperm(w.num_blocks, generator=gen, device=device)[:tokens // w.block_size]
+    patterns = {
+        "block_slots": (blocks[:, None] * w.block_size
+                        + torch.arange(w.block_size, device=device)).reshape(-1),
+        "random_slots": torch.randperm(num_slots, generator=gen, device=device)[:tokens],
+    }
     per_step = w.layers * tokens * (4 * kv_width * 2 + 4)
     out = {"tokens": tokens, "layers": w.layers, "algorithmic_bytes_per_step": per_step}
-    # Eager: one Python call per layer, as in a prefill forward. Graph: the same
-    # 36 launches captured in a CUDA graph, which isolates the kernel from the
-    # host launch path (decode steps run this way under the engine's graphs).
-    side = torch.cuda.Stream(device)
-    side.wait_stream(torch.cuda.current_stream(device))
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(side):
-        ours()
-        with torch.cuda.graph(graph, stream=side):
-            ours()
-    torch.cuda.current_stream(device).wait_stream(side)
     stream = torch.cuda.current_stream(device)
-    for name, fn in (("kvoff_eager", ours), ("kvoff_graph", graph.replay),
-                     ("torch_index_put", torch_scatter)):
-        ms = Timer(torch, stream, 1).run(fn, args.steps, args.warmup) / args.steps
-        out[name] = {"ms_per_step": ms, "GBps": per_step / (ms / 1e3) / 1e9,
-                     "us_per_launch": 1e3 * ms / w.layers}
-    out["kvoff_graph"]["frac_of_hbm_peak"] = out["kvoff_graph"]["GBps"] / hbm_peak
-    del graph
-    ops.store_kvcache(keys[0], values[0], caches[0, 0], caches[1, 0], slots, bad_slots=bad)
+    bad = torch.zeros(1, dtype=torch.int32, device=device)
+    for pattern, slots in patterns.items():
+        slots = slots.to(torch.int32).contiguous()
+        slots[::97] = -1  # padded positions are skipped
+
+        def ours(slots=slots):
+            for layer in range(w.layers):
+                ops.store_kvcache(keys[layer], values[layer], caches[0, layer],
+                                  caches[1, layer], slots)
+
+        valid = slots >= 0
+        idx = slots[valid].long()
+
+        def torch_scatter(valid=valid, idx=idx):  # the reference kernel's semantics
+            for layer in range(w.layers):
+                caches[0, layer].view(-1, kv_width)[idx] = keys[layer].reshape(tokens, -1)[valid]
+                caches[1, layer].view(-1, kv_width)[idx] = values[layer].reshape(tokens, -1)[valid]
+
+        # Eager: one Python call per layer, as in a prefill forward. Graph: the
+        # same 36 launches captured in a CUDA graph, which isolates the kernel
+        # from the host launch path (decode steps run this way under the
+        # engine's graphs).
+        side = torch.cuda.Stream(device)
+        side.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            ours()
+            with torch.cuda.graph(graph, stream=side):
+                ours()
+        stream.wait_stream(side)
+        res = {}
+        for name, fn in (("kvoff_eager", ours), ("kvoff_graph", graph.replay),
+                         ("torch_index_put", torch_scatter)):
+            ms = Timer(torch, stream, 1).run(fn, args.steps, args.warmup) / args.steps
+            res[name] = {"ms_per_step": ms, "GBps": per_step / (ms / 1e3) / 1e9,
+                         "us_per_launch": 1e3 * ms / w.layers}
+        res["kvoff_graph"]["frac_of_hbm_peak"] = res["kvoff_graph"]["GBps"] / hbm_peak
+        del graph
+        ops.store_kvcache(keys[0], values[0], caches[0, 0], caches[1, 0], slots, bad_slots=bad)
+        out[pattern] = res
     torch.cuda.synchronize()
     out["bad_slots"] = int(bad.item())
     del keys, values, qkv
