@@ -875,7 +875,12 @@ def run_ours(args) -> None:
         "roofline": roofline,
         "cpu_baseline": cpu,
         "clocks": clocks_e2e.summary() or clocks_dev.summary(),
-        "gpu_launches": launches * args.steps,
+        # kvoff kernels launched inside the two timed regions (device step: one
+        # save and one restore launch per 128 blocks; e2e: one kernel per
+        # staging half, or per 128 blocks for mapped slots).
+        "gpu_launches": (2 * launches_per_call + launches) * args.steps,
+        "gpu_launches_by_region": {"value": 2 * launches_per_call * args.steps,
+                                   "e2e": launches * args.steps},
         "pcie_memcpy_ceiling_GBps": ceiling,
         "sweep_GBps": sweep,
         "dropin_e2e_GBps": dropin,

@@ -10,13 +10,13 @@
 // striding over the units (restore 88 % -> 99 % of the measured copy peak,
 // save 95 % -> 100 %). The kernels still stride, so a max_ctas cap is valid.
 //
-// Save, fast path (D = 8 * LANES, LANES in {4, 8, 16, 32}): LANES lanes own
-// one row, each loading 16 bytes (8 bf16) with a non-coherent streaming load.
-// The row amax is an integer max over |bf16| bit patterns (exact, and NaN
-// wins because NaN patterns sort above Inf), reduced with xor-shuffles inside
-// the lane group. Each lane then writes 8 payload bytes; the tile's scales are
-// collected in shared memory and written as one contiguous run, which keeps
-// zero-copy (PCIe) scale writes coalesced.
+// Save, fast path (D = 16 * LANES, LANES in {2, 4, 8, 16}): LANES lanes own
+// one row, each loading two 16-byte pieces (16 bf16) with non-coherent
+// streaming loads. The row amax is an integer max over |bf16| bit patterns
+// (exact, and NaN wins because NaN patterns sort above Inf), reduced with
+// xor-shuffles inside the lane group. Each lane then writes 16 payload bytes;
+// the tile's scales are collected in shared memory and written as one
+// contiguous run, which keeps zero-copy (PCIe) scale writes coalesced.
 #include <cuda_runtime.h>
 #include <stdint.h>
 

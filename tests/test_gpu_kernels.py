@@ -59,9 +59,11 @@ def empty_slots(n: int, g, device):
     return payload, scale
 
 
-@pytest.mark.parametrize("d,heads,block_size", [(128, 8, 256), (64, 4, 64), (256, 2, 32),
-                                               (32, 3, 16), (4, 1, 256), (8, 2, 16),
-                                               (80, 2, 16)])
+# Config-2 heads, config-4 per-rank shards (tp=8: 1 KV head; tp=2: 4), and odd
+# head dims and block sizes that take the generic kernels.
+@pytest.mark.parametrize("d,heads,block_size", [(128, 8, 256), (128, 1, 256), (128, 4, 256),
+                                               (64, 4, 64), (256, 2, 32), (32, 3, 16),
+                                               (4, 1, 256), (8, 2, 16), (80, 2, 16)])
 def test_fp8_save_restore_bit_exact(cuda, d, heads, block_size):
     from kvoff import ops
 
