@@ -98,21 +98,28 @@ def test_tiny_pool_round_trips_match_reference_cache():
 
 
 def test_config1_digests_match_reference_cache():
+    """All 16 config-1 blocks against the reference cache's per-block digests.
+
+    The digests are per block (each saved slot, each restored target), so the
+    blocks are checked one at a time in a reused one-block pool instead of the
+    full 1.9 GB config-1 pool.
+    """
     golden = json.loads((GOLDEN / "config1.json").read_text())
     c = golden["config"]
     sources, targets = golden["sources"], golden["targets"]
     assert [sources, targets] == list(workloads.config1_ids(c["seed"], c["num_blocks"],
                                                             c["saved"]))
-    pool = workloads.pool_with_blocks(sources, c["layers"], c["num_blocks"], c["block_size"],
-                                      c["heads"], c["head_dim"], c["seed"])
-    payload, scale = oracle.fp8_save_blocks(pool, sources)
-    assert [sha(p) for p in payload] == golden["fp8"]["payload_sha256"]
-    assert [sha(s) for s in scale] == golden["fp8"]["scale_sha256"]
-    oracle.fp8_restore_blocks(pool, targets, payload, scale)
-    assert [sha(pool[:, :, t]) for t in targets] == golden["fp8"]["restored_sha256"]
-    # BF16 slots are the blocks' own bytes.
-    slots = oracle.copy_blocks(pool, sources)
-    assert [sha(s) for s in slots] == golden["bf16"]["payload_sha256"]
+    mask = workloads.outlier_mask(c["layers"], c["heads"], c["head_dim"], c["seed"])
+    block = np.empty((2, c["layers"], 1, c["block_size"], c["heads"], c["head_dim"]), np.uint16)
+    for i, source in enumerate(sources):
+        block[:, :, 0] = workloads.block_values(source, c["layers"], c["block_size"], c["heads"],
+                                                c["head_dim"], c["seed"], mask)
+        assert sha(oracle.copy_blocks(block, [0])[0]) == golden["bf16"]["payload_sha256"][i]
+        payload, scale = oracle.fp8_save_blocks(block, [0])
+        assert sha(payload[0]) == golden["fp8"]["payload_sha256"][i]
+        assert sha(scale[0]) == golden["fp8"]["scale_sha256"][i]
+        oracle.fp8_restore_blocks(block, [0], payload, scale)  # slot i -> targets[i]
+        assert sha(block[:, :, 0]) == golden["fp8"]["restored_sha256"][i]
     assert golden["fp8"]["within_amax_over_16"]
 
 

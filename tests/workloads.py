@@ -19,9 +19,17 @@ CONFIG2 = dict(layers=36, num_blocks=320, block_size=256, heads=8, head_dim=128)
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
-    """float32 -> bf16 bit patterns, round to nearest even (finite inputs)."""
-    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    """float32 -> bf16 bit patterns, round to nearest even (finite inputs).
+
+    In-place uint32 arithmetic: a finite pattern plus the rounding increment
+    stays below 2**32, and no wide temporaries are allocated.
+    """
+    u = np.array(x, dtype=np.float32, copy=True).view(np.uint32)
+    odd = (u >> 16) & 1
+    u += np.uint32(0x7FFF)
+    u += odd
+    u >>= 16
+    return u.astype(np.uint16)
 
 
 def outlier_mask(layers: int, heads: int, head_dim: int, seed: int,
