@@ -90,3 +90,35 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIBRARY", tmp_path / "libkvoff.so")
     with pytest.raises(RuntimeError, match="not built"):
         _lib.lib()
+
+
+def test_event_ordered_entry_points_check_their_arguments_on_the_host():
+    so = _lib.lib()
+    ids = _lib.int64_array([0])
+    slots = _lib.pointer_array([16])
+    # A wait-event count with no list is rejected before any device work.
+    rc = so.kvoff_fp8_save_blocks_staged_ev(ctypes.c_void_p(256), 4, 4096, 1024, 4, 8, 128, ids,
+                                            1, slots, slots, ctypes.c_void_p(512),
+                                            ctypes.c_void_p(512), 2, None, 1, None, None)
+    assert rc == _lib.KVOFF_EINVAL and "wait event" in _lib.last_error()
+    rc = so.kvoff_fp8_save_blocks_staged_ev(ctypes.c_void_p(256), 4, 4096, 1024, 4, 8, 128, ids,
+                                            1, slots, slots, ctypes.c_void_p(512),
+                                            ctypes.c_void_p(512), 2, None, -1, None, None)
+    assert rc == _lib.KVOFF_EINVAL
+    # Empty batches are a no-op; out-of-range ids fail like the plain staged calls.
+    assert so.kvoff_fp8_restore_blocks_staged_ev(ctypes.c_void_p(256), 4, 4096, 1024, 4, 8, 128,
+                                                 ids, 0, slots, slots, None, None, 2, None,
+                                                 None) == _lib.KVOFF_OK
+    bad = _lib.int64_array([9])
+    rc = so.kvoff_fp8_restore_blocks_staged_ev(ctypes.c_void_p(256), 4, 4096, 1024, 4, 8, 128,
+                                               bad, 1, slots, slots, ctypes.c_void_p(512),
+                                               ctypes.c_void_p(512), 2, None, None)
+    assert rc == _lib.KVOFF_EINVAL and "out of range" in _lib.last_error()
+
+
+def test_ops_rejects_events_that_were_never_recorded():
+    from kvoff import ops
+
+    with pytest.raises(ValueError, match="recorded"):
+        ops._event(0)
+    assert ops._event(1234) == 1234
