@@ -79,6 +79,15 @@ KVOFF_API int kvoff_debug_fail_next(const char* op, int32_t count);
 KVOFF_API int kvoff_device_error(int32_t device, int32_t* flags, int32_t clear);
 
 /*
+ * Test hook for the bounded-wait error path (no counterpart in the
+ * reference): enqueues one thread that waits on an mbarrier nothing arrives
+ * at, gives up after limit_ns (at most 2 s), and sets the same flag as a
+ * timed-out TMA copy wait. The context stays usable; kvoff_device_error
+ * reads the flag.
+ */
+KVOFF_API int kvoff_debug_bounded_wait(int64_t limit_ns, void* stream);
+
+/*
  * FP8 save: gather `count` KV blocks of a bf16 paged pool and quantize each
  * row to float8_e4m3fn with one bf16 scale per row:
  *     scale   = bf16_rne(max(f32(amax|x|) / 448, 1e-30))

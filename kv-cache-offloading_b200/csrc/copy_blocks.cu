@@ -64,13 +64,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
-// Waits for phase `parity` of the mbarrier for at most kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+// Waits for phase `parity` of the mbarrier for at most limit_ns of
+// %globaltimer, and at most kMaxSpins polls whatever the timer does.
+constexpr uint64_t kMaxSpins = 1ull << 24;
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_ns();
-  while (!mbar_try_wait(bar, parity))
-    if (global_ns() - start > kWaitLimitNs) return false;
+  for (uint64_t spins = 0; !mbar_try_wait(bar, parity); ++spins)
+    if (spins >= kMaxSpins || global_ns() - start > limit_ns) return false;
   return true;
+}
+
+// Test hook for the bounded-wait error path: one thread waits on an mbarrier
+// that nothing arrives at, gives up after limit_ns, and reports it in
+// g_device_error exactly as tma_copy_kernel does.
+__global__ void __launch_bounds__(32) debug_bounded_wait_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&bar)) : "memory");
+  if (!mbar_wait_bounded(smem_addr(&bar), 0, limit_ns))
+    atomicOr(&g_device_error, kErrTmaWaitTimeout);
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_addr(&bar)) : "memory");
 }
 
 __device__ __forceinline__ void tma_load(uint32_t dst_smem, const void* src, uint32_t bytes,
@@ -363,6 +379,15 @@ int kvoff_copy_tokens(void* pool, int64_t num_chunks, int64_t chunk_stride_bytes
                                 num_chunks, cudaMemcpyDefault, s);
     KVOFF_TRY(cuda_status(e, "cudaMemcpy2DAsync (token copy)"));
   }
+  return ok();
+}
+
+int kvoff_debug_bounded_wait(int64_t limit_ns, void* stream) {
+  if (limit_ns <= 0 || limit_ns > 2000000000ll)
+    return fail(KVOFF_EINVAL, "kvoff_debug_bounded_wait: limit must be in (0, 2 s]");
+  debug_bounded_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      (uint64_t)limit_ns);
+  KVOFF_TRY(cuda_status(cudaGetLastError(), "debug_bounded_wait launch"));
   return ok();
 }
 

@@ -122,3 +122,10 @@ def test_ops_rejects_events_that_were_never_recorded():
     with pytest.raises(ValueError, match="recorded"):
         ops._event(0)
     assert ops._event(1234) == 1234
+
+
+def test_bounded_wait_hook_rejects_limits_outside_its_range():
+    so = _lib.lib()
+    assert so.kvoff_debug_bounded_wait(0, None) == _lib.KVOFF_EINVAL
+    assert so.kvoff_debug_bounded_wait(3_000_000_000, None) == _lib.KVOFF_EINVAL
+    assert "limit" in _lib.last_error()

@@ -247,6 +247,25 @@ def test_bf16_passthrough_byte_exact(cuda, method, shape):
     assert device_error(0) == 0
 
 
+def test_bounded_device_wait_reports_a_timeout_and_the_context_survives(cuda):
+    """A device-side wait that nothing satisfies gives up after its limit and
+    sets the flag the host reads; the context keeps working afterwards."""
+    from kvoff import _lib, device_error, ops
+
+    assert device_error(0) == 0
+    stream = torch.cuda.current_stream(cuda)
+    _lib.call("kvoff_debug_bounded_wait", 20_000_000, stream.cuda_stream)  # 20 ms
+    assert device_error(0) & 1  # synchronizes, reads and clears
+    assert device_error(0) == 0
+    pool = torch.randint(-2 ** 15, 2 ** 15, (2, 2, 4, 16, 2, 64), dtype=torch.int16,
+                         device=cuda).view(torch.bfloat16)
+    g = ops.geometry(pool)
+    slot = torch.empty(g.block_bytes, dtype=torch.uint8, device=cuda)
+    ops.copy_blocks(pool, [3], [slot.data_ptr()], method=ops.COPY_TMA)
+    assert torch.equal(slot.view(torch.int16), pool[:, :, 3].contiguous().view(torch.int16).reshape(-1))
+    assert device_error(0) == 0
+
+
 @pytest.mark.parametrize("name", sorted(workloads.STORE_CASES))
 def test_store_kvcache_matches_oracle_and_fixture(cuda, name):
     from kvoff import ops
