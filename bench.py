@@ -534,6 +534,21 @@ def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, mai
             cache.discard(h)
     out.update({name: statistics.median(v) for name, v in waits.items()})
     # The hybrid planner's restore cost at the batch sizes admission restores.
+    # Host time per drop-in call (the engine thread's cost; the GPU work is
+    # asynchronous): 64 save_block calls, then 64 _copy_entry calls.
+    n = min(64, B)
+    main.synchronize()
+    t0 = time.perf_counter()
+    for h in saves[:n]:
+        cache.save_block(h)
+    t1 = time.perf_counter()
+    for e, b in zip(entries[:n], restore_ids[:n]):
+        cache._copy_entry(e, b, wait=False)
+    t2 = time.perf_counter()
+    join()
+    main.synchronize()
+    out["host_us_per_call"] = {"save_block": 1e6 * (t1 - t0) / n,
+                               "_copy_entry": 1e6 * (t2 - t1) / n}
     out["restore_ms_per_block"] = {
         str(b): 1e3 * cache.measure_restore_s_per_block(repeats=max(1, 64 // b), batch=b)
         for b in SWEEP_BATCHES if b <= B}

@@ -24,6 +24,8 @@ torch copies and quantizer below.
 
 from __future__ import annotations
 
+import contextlib
+
 import os
 from dataclasses import dataclass
 from math import prod
@@ -181,6 +183,9 @@ class CPUBlockCache:
         self._slab_owners: list = []  # PinnedSlab per chunk (CUDA pools)
         self._free_slots: list[int] = []
         self._num_slots = 0
+        self._slot_loc: list[tuple[int, int]] = []  # slot -> (slab chunk, index in it)
+        # slot -> (payload, scale) host pointers and their device aliases (CUDA pools)
+        self._slot_ptrs: list[tuple[int, int, int, int]] = []
         self._on_cuda = pool.device.type == "cuda"
         self._copy_stream = self._restore_stream = None
         self._slot_reads: dict[int, torch.cuda.Event] = {}  # slot -> last restore reading it
@@ -202,6 +207,7 @@ class CPUBlockCache:
             self._copy_stream = torch.cuda.Stream(pool.device)
             self._restore_stream = (torch.cuda.Stream(pool.device) if split_streams
                                     else self._copy_stream)
+            self._ready = torch.cuda.Event()  # re-recorded before each staged save
 
     # -- tensor parallelism ----------------------------------------------------
     #
@@ -346,19 +352,26 @@ class CPUBlockCache:
             payload = torch.empty((count, *self._shape), dtype=self._dtype, device="cpu")
             scales = (torch.empty((count, *self._scale_shape), dtype=self._cache.dtype,
                                   device="cpu") if self._fp8 else None)
+        chunk = len(self._slabs)
         self._slabs.append(payload)
         if self._fp8:
             self._scale_slabs.append(scales)
+        self._slot_loc.extend((chunk, i) for i in range(count))
+        if self._on_cuda:
+            pb, sb = self._payload_bytes, self._scale_bytes
+            p0, pa = payload.data_ptr(), slab.device_alias(payload)
+            s0, sa = (scales.data_ptr(), slab.device_alias(scales)) if self._fp8 else (0, 0)
+            self._slot_ptrs.extend(
+                (p0 + i * pb, s0 + i * sb if sb else 0, pa + i * pb, sa + i * sb if sb else 0)
+                for i in range(count))
         first = self._num_slots
         self._free_slots.extend(range(first + count - 1, first - 1, -1))
         self._num_slots += count
 
     def _locate(self, slot: int) -> tuple[int, int]:
-        for chunk, slab in enumerate(self._slabs):
-            if slot < len(slab):
-                return chunk, slot
-            slot -= len(slab)
-        raise IndexError(slot)
+        if slot < 0:
+            raise IndexError(slot)
+        return self._slot_loc[slot]
 
     def _slot_view(self, slot: int) -> tuple[torch.Tensor, torch.Tensor | None]:
         chunk, index = self._locate(slot)
@@ -380,24 +393,19 @@ class CPUBlockCache:
             device = self._cache.device
             if staged is not None:  # kernels of earlier calls may still use it
                 self._ops.join_pipeline(device, stream)
-            scales = (torch.empty((want, self._scale_bytes), dtype=torch.uint8, device=device)
-                      if self._fp8 else None)
-            staged = (torch.empty((want, self._payload_bytes), dtype=torch.uint8, device=device),
-                      scales)
+            with torch.cuda.stream(stream):  # owned by, and reused in order on, `stream`
+                scales = (torch.empty((want, self._scale_bytes), dtype=torch.uint8,
+                                      device=device) if self._fp8 else None)
+                staged = (torch.empty((want, self._payload_bytes), dtype=torch.uint8,
+                                      device=device), scales)
             self._staging[stream] = staged
         return staged
 
     # -- device copies (CUDA pools) ---------------------------------------------
 
     def _slot_pointers(self, slot: int, mapped: bool) -> tuple[int, int]:
-        chunk, index = self._locate(slot)
-        payload = self._slabs[chunk][index]
-        scale = self._scale_slabs[chunk][index] if self._fp8 else None
-        if not mapped:
-            return payload.data_ptr(), scale.data_ptr() if scale is not None else 0
-        owner = self._slab_owners[chunk]
-        return (owner.device_alias(payload),
-                owner.device_alias(scale) if scale is not None else 0)
+        payload, scale, payload_alias, scale_alias = self._slot_ptrs[slot]
+        return (payload_alias, scale_alias) if mapped else (payload, scale)
 
     def _pointers(self, slots, mapped: bool) -> tuple[list[int], list[int]]:
         pairs = [self._slot_pointers(slot, mapped) for slot in slots]
@@ -416,9 +424,8 @@ class CPUBlockCache:
             if mapped:
                 ops.save_fp8(pool, block_ids, payload, scale, stream=stream)
             else:
-                ops.save_fp8_staged(pool, block_ids, payload, scale,
-                                    *self._stage(stream, len(block_ids)), stream=stream,
-                                    wait_events=wait_events, source_done=source_done)
+                self._staged_call(True, pool, block_ids, payload, scale, stream,
+                                  wait_events or (), source_done)
             return
         method = modes["bf16_save"]
         payload, _ = self._pointers(slots, method == "sm")
@@ -445,9 +452,7 @@ class CPUBlockCache:
             if modes["fp8_restore"] == "mapped":
                 ops.restore_fp8(pool, block_ids, *mapped, stream=stream)
             else:
-                ops.restore_fp8_staged(pool, block_ids, *plain,
-                                       *self._stage(stream, len(block_ids)), stream=stream,
-                                       done_event=done_event)
+                self._staged_call(False, pool, block_ids, *plain, stream, (), done_event)
             return
         method = modes["bf16_restore"]
         if method == "tma":
@@ -464,6 +469,24 @@ class CPUBlockCache:
                             stream=stream)
         else:
             ops.copy_blocks(pool, block_ids, plain[0], restore=True, stream=stream)
+
+    def _staged_call(self, save: bool, pool: torch.Tensor, block_ids, payload, scale, stream,
+                     wait_events, event):
+        """One staged FP8 call through ops._fp8_staged_ev (raw handles, the
+        cache's own geometry, no per-call tensor checks). wait_events and
+        event are recorded torch.cuda.Events or None."""
+        staged_payload, staged_scale = self._stage(stream, len(block_ids))
+        g = self._geometry if pool is self._cache else self._ops.geometry(pool)
+        waits = [e.cuda_event for e in wait_events]
+        index = pool.device.index
+        guard = (contextlib.nullcontext() if torch.cuda.current_device() == index
+                 else torch.cuda.device(index))
+        with guard:
+            self._ops._fp8_staged_ev(save, g, pool.data_ptr(), block_ids, payload, scale,
+                                     staged_payload.data_ptr(), staged_scale.data_ptr(),
+                                     min(staged_payload.shape[0], staged_scale.shape[0]),
+                                     stream.cuda_stream, waits,
+                                     event.cuda_event if event is not None else 0)
 
     def _restore_slots(self, slots, block_ids, stream) -> torch.cuda.Event:
         """Restore slots into pool blocks on `stream`; returns the done event.
@@ -671,7 +694,8 @@ class CPUBlockCache:
         if staged:
             # The kernels wait only for the blocks' writers (and restores still
             # filling them), not for earlier saves' copies on the copy stream.
-            ready = torch.cuda.Event()
+            # One event serves every call: a wait takes its latest record.
+            ready = self._ready
             ready.record(current)
             waits = [ready]
             for block_id in dict.fromkeys(block_ids):
@@ -686,10 +710,9 @@ class CPUBlockCache:
             slot_read = self._slot_reads.pop(slot, None)
             if slot_read is not None and self._restore_stream is not copy:
                 copy.wait_event(slot_read)
-        with torch.cuda.stream(copy):
-            self._device_save(pool, list(block_ids), list(slots), copy, waits, read)
-            done = torch.cuda.Event()
-            done.record(copy)
+        self._device_save(pool, list(block_ids), list(slots), copy, waits, read)
+        done = torch.cuda.Event()
+        done.record(copy)
         for block_id in block_ids:
             self._pending_saves[block_id] = read if read is not None else done
         self._rpc("save", list(block_ids), list(slots))
@@ -753,8 +776,7 @@ class CPUBlockCache:
         stream.wait_stream(current)
         if entry.saved is not None and stream is not self._copy_stream:
             stream.wait_event(entry.saved)
-        with torch.cuda.stream(stream):
-            done = self._restore_slots([entry.slot], [block_id], stream)
+        done = self._restore_slots([entry.slot], [block_id], stream)
         self._slot_reads[entry.slot] = done
         if wait:
             current.wait_event(done)
@@ -792,8 +814,7 @@ class CPUBlockCache:
                 if entry.saved is not None and id(entry.saved) not in waited:
                     waited.add(id(entry.saved))
                     stream.wait_event(entry.saved)
-        with torch.cuda.stream(stream):
-            done = self._restore_slots([e.slot for e in entries], block_ids, stream)
+        done = self._restore_slots([e.slot for e in entries], block_ids, stream)
         for entry in entries:
             self._slot_reads[entry.slot] = done
         if wait:

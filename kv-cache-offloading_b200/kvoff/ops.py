@@ -8,6 +8,7 @@ pointers so that one call can target pinned host slabs, their device aliases
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -196,6 +197,39 @@ def restore_fp8_staged(pool: torch.Tensor, block_ids, host_payload_ptrs, host_sc
         else:
             _lib.call("kvoff_fp8_restore_blocks_staged_ev", *common, _event(done_event),
                       _stream(pool.device, stream))
+
+
+def _fp8_staged_ev(save: bool, g: PoolGeometry, pool_ptr: int, block_ids, payload_ptrs,
+                   scale_ptrs, staging_payload_ptr: int, staging_scale_ptr: int,
+                   staging_blocks: int, stream: int, wait_events=(), event: int = 0) -> None:
+    """Lean form of save_fp8_staged / restore_fp8_staged for a caller that
+    already holds a checked geometry, raw pointers, raw stream and event
+    handles, and has the pool's device current (the drop-in cache's per-block
+    path, which runs once per saved or restored block on the engine thread).
+
+    Save: the kernels wait for `wait_events` (none: all earlier work on the
+    stream) and `event`, when non-zero, is recorded once the pool blocks are
+    read. Restore: `event`, when non-zero, is recorded after the last pool
+    write and the stream is not joined (see restore_fp8_staged).
+    """
+    so = _lib.lib()
+    n = len(block_ids)
+    ids = (ctypes.c_int64 * n)(*block_ids)
+    payload = (ctypes.c_void_p * n)(*payload_ptrs)
+    scale = (ctypes.c_void_p * n)(*scale_ptrs)
+    if save:
+        waits = (ctypes.c_void_p * max(1, len(wait_events)))(*wait_events)
+        rc = so.kvoff_fp8_save_blocks_staged_ev(
+            pool_ptr, g.num_chunks, g.chunk_stride, g.block_stride, g.num_blocks,
+            g.rows_per_chunk, g.head_dim, ids, n, payload, scale, staging_payload_ptr,
+            staging_scale_ptr, staging_blocks, waits, len(wait_events), event or None, stream)
+        _lib.check(rc, "kvoff_fp8_save_blocks_staged_ev")
+    else:
+        rc = so.kvoff_fp8_restore_blocks_staged_ev(
+            pool_ptr, g.num_chunks, g.chunk_stride, g.block_stride, g.num_blocks,
+            g.rows_per_chunk, g.head_dim, ids, n, payload, scale, staging_payload_ptr,
+            staging_scale_ptr, staging_blocks, event or None, stream)
+        _lib.check(rc, "kvoff_fp8_restore_blocks_staged_ev")
 
 
 def join_pipeline(device, stream=None) -> None:
