@@ -45,7 +45,8 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent))
 import workloads  # noqa: E402
 
-REFERENCE = Path(os.environ.get("KVOFF_REFERENCE", "/root/reference"))
+# The reference checkout: KVOFF_REFERENCE, else a "reference" directory beside this repository.
+REFERENCE = Path(os.environ.get("KVOFF_REFERENCE", HERE.parents[2] / "reference"))
 ENGINE_ROOT = REFERENCE / "nanovllm_upstream" / "nanovllm"
 
 

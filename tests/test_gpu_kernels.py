@@ -198,6 +198,52 @@ def test_fp8_staged_pipeline_over_many_groups_and_calls(cuda):
     assert np.array_equal(u16(pool), bits)
 
 
+def test_fp8_event_ordered_staged_calls(cuda):
+    """The _ev entry points through the public wrappers: kernels ordered on
+    given events, a source-read event, a restore done event, and a join."""
+    from kvoff import ops
+    from kvoff.slab import PinnedSlab
+
+    bits = special_pool(2, 10, 128, 8, 128, seed=8)
+    pool = to_bf16(bits, cuda)
+    g = ops.geometry(pool)
+    per = g.fp8_payload_bytes + g.fp8_scale_bytes
+    slab = PinnedSlab(6 * per, device=0)
+    payload = [slab.view(i * g.fp8_payload_bytes, (g.fp8_payload_bytes,), torch.uint8)
+               for i in range(6)]
+    scale = [slab.view(6 * g.fp8_payload_bytes + i * g.fp8_scale_bytes, (g.fp8_scale_bytes,),
+                       torch.uint8) for i in range(6)]
+    staging = empty_slots(2, g, cuda)
+    stream = torch.cuda.Stream(cuda)
+    ids = [9, 2, 5, 0, 7, 3]
+    want_p, want_s = oracle.fp8_save_blocks(bits, ids)
+    written = torch.cuda.Event()
+    written.record(torch.cuda.current_stream(cuda))
+    read = torch.cuda.Event()
+    read.record(stream)
+    for i in range(6):  # one block per call: kernels overlap the previous call's copies
+        ops.save_fp8_staged(pool, [ids[i]], [payload[i].data_ptr()], [scale[i].data_ptr()],
+                            *staging, stream=stream, wait_events=[written], source_done=read)
+    torch.cuda.current_stream(cuda).wait_event(read)
+    pool[:, :, ids[-1]].fill_(1.0)  # the last block is rewritten once it has been read
+    stream.synchronize()
+    for i in range(6):
+        assert np.array_equal(payload[i].numpy(), want_p[i].reshape(-1))
+        assert np.array_equal(scale[i].numpy().view(np.uint16), want_s[i].reshape(-1))
+    targets = [1, 4, 6, 8, 9, 2]
+    done = torch.cuda.Event()
+    done.record(stream)
+    for i in range(6):
+        ops.restore_fp8_staged(pool, [targets[i]], [payload[i].data_ptr()],
+                               [scale[i].data_ptr()], *staging, stream=stream, done_event=done)
+    ops.join_pipeline(cuda, stream)
+    stream.synchronize()
+    oracle.fp8_restore_blocks(bits, targets, want_p, want_s)
+    got = u16(pool)
+    for t in targets:
+        assert np.array_equal(got[:, :, t], bits[:, :, t])
+
+
 def test_fp8_batches_larger_than_one_launch(cuda):
     from kvoff import ops
 

@@ -19,7 +19,8 @@ from pathlib import Path
 import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
-REFERENCE = Path(os.environ.get("KVOFF_REFERENCE", "/root/reference"))
+# The reference checkout: KVOFF_REFERENCE, else a "reference" directory beside this repository.
+REFERENCE = Path(os.environ.get("KVOFF_REFERENCE", ROOT.parent / "reference"))
 KVOFF = ROOT / "kv-cache-offloading_b200" / "kvoff"
 DROPINS = {"cpu_prefix_cache.py": KVOFF / "cpu_prefix_cache.py",
            "kv_handoff.py": KVOFF / "kv_handoff.py"}
