@@ -118,6 +118,8 @@ def parse_args():
     p.add_argument("--no-sweep", action="store_true", help="skip the batch-size / mode sweep")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-store", action="store_true", help="skip the store_kvcache measurement")
+    p.add_argument("--no-handoff", action="store_true",
+                   help="skip the KV handoff export / import measurement")
     p.add_argument("--no-dropin", action="store_true",
                    help="skip the per-block vs batched CPUBlockCache measurement")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
@@ -447,6 +449,70 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
     torch.cuda.synchronize()
     out["bad_slots"] = int(bad.item())
     del keys, values, qkv
+    return out
+
+
+def handoff_bench(torch, w: Workload, pool, args) -> dict:
+    """KV handoff of one sequence (nanovllm/engine/kv_handoff.py:34-135): export
+    its written tokens from 32 random pool blocks into a dense host snapshot
+    [2, L, tokens, H, D], and import a snapshot into 32 other blocks. 8191
+    tokens, so the last block is partial. Ours: one strided DMA per block
+    between the pool and pinned memory (ops.copy_tokens, what the drop-in
+    export_kv / import_kv run). Reference path, as torch ops on this GPU:
+    index_select + contiguous + pageable .cpu(), and .to(device) + one copy_ per
+    block. Both are timed with the host waiting for the result, as export_kv
+    returns a finished snapshot; the exported bytes are checked equal.
+    """
+    from kvoff import ops
+
+    device = pool.device
+    nblocks = 32
+    count = nblocks * w.block_size - 1
+    gen = torch.Generator().manual_seed(11)
+    perm = torch.randperm(w.num_blocks, generator=gen)
+    src, dst = perm[:nblocks].tolist(), perm[nblocks:2 * nblocks].tolist()
+    shape = (2, w.layers, count, w.heads, w.head_dim)
+    nbytes = 2 * w.layers * count * w.heads * w.head_dim * pool.element_size()
+    pinned = torch.empty(shape, dtype=pool.dtype, pin_memory=True)
+    index = torch.tensor(src, dtype=torch.int64, device=device)
+
+    def ours_export():
+        ops.copy_tokens(pool, src, count, pinned.data_ptr())
+        torch.cuda.current_stream(device).synchronize()
+
+    def ours_import():
+        ops.copy_tokens(pool, dst, count, pinned.data_ptr(), restore=True)
+        torch.cuda.current_stream(device).synchronize()
+
+    snapshot = {}
+
+    def ref_export():
+        packed = pool.index_select(2, index).flatten(2, 3)
+        snapshot["kv"] = packed[:, :, :count].contiguous().cpu()
+
+    def ref_import():
+        payload = snapshot["kv"].to(device=device)
+        for logical, physical in enumerate(dst):
+            start = logical * w.block_size
+            end = min(start + w.block_size, count)
+            pool[:, :, physical, :end - start].copy_(payload[:, :, start:end])
+        torch.cuda.current_stream(device).synchronize()
+
+    def seconds(fn, reps=5):
+        fn()
+        t = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t) / reps
+
+    out = {"tokens": count, "blocks": nblocks, "bytes": nbytes}
+    for name, fn in (("kvoff_export", ours_export), ("kvoff_import", ours_import),
+                     ("torch_export", ref_export), ("torch_import", ref_import)):
+        sec = seconds(fn)
+        out[name] = {"ms": 1e3 * sec, "GBps": nbytes / sec / 1e9}
+    out["export_bytes_equal"] = bool(torch.equal(pinned.view(torch.int16),
+                                                 snapshot["kv"].view(torch.int16)))
+    del pinned, snapshot
     return out
 
 
@@ -806,6 +872,10 @@ def run_ours(args) -> None:
     store = store_kvcache_bench(torch, w, pool, args, hbm_peak) \
         if single and not args.no_store else None
 
+    # ---- KV handoff export / import of one sequence ---------------------------
+    handoff = handoff_bench(torch, w, pool, args) \
+        if single and not args.no_handoff and w.num_blocks >= 64 else None
+
     # ---- through the drop-in CPUBlockCache: per-block calls vs batched calls ----
     dropin = dropin_e2e(torch, w, pool, save_ids, restore_ids, args, timer, main) \
         if single and w.batch <= 256 and not args.no_dropin else None
@@ -900,6 +970,7 @@ def run_ours(args) -> None:
         "sweep_GBps": sweep,
         "dropin_e2e_GBps": dropin,
         "store_kvcache": store,
+        "kv_handoff": handoff,
         "reference_gpu_path": ref_gpu,
     }
     if rank == 0:
