@@ -222,6 +222,20 @@ class ClockSampler:
 _CPU_STATE: dict = {}
 
 
+def host_cpu() -> dict:
+    """The host CPU the baseline ran on (model, usable and logical CPUs)."""
+    model = ""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"model": model, "affinity_cpus": len(os.sched_getaffinity(0)),
+            "logical_cpus": os.cpu_count()}
+
+
 def cpu_sample(w: Workload, seconds: float, threads: int | None = None) -> dict:
     """Save + restore FP8 blocks of the workload's shape on the host cores."""
     import numpy as np
@@ -259,7 +273,7 @@ def cpu_sample(w: Workload, seconds: float, threads: int | None = None) -> dict:
             "sample": f"{iters} x (FP8 save of 2 + restore of 2 blocks of the workload shape), "
                       f"{elapsed:.1f} s on {cores} OpenMP threads",
             "tokens_per_s": iters * 4 * w.block_size / elapsed,
-            "ms_per_block": 1000 * elapsed / (iters * 4)}
+            "ms_per_block": 1000 * elapsed / (iters * 4), "host": host_cpu()}
 
 
 def torch_ops_sample(w: Workload, seconds: float) -> dict:
@@ -301,11 +315,14 @@ def run_reference(args) -> None:
           "ms_per_step": statistics.mean(s["ms_per_block"] for s in samples) * 4,
           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
           "data": "synthetic N(0,1), seed 0",
-          "config": {"workload": w.describe(), "batch_blocks": 2,
+          "config": {"workload": w.describe(), "batch_blocks": w.batch,
+                     "pool_blocks": w.num_blocks, "sample_blocks_per_step": 4,
                      "note": "host-core sample of the workload: each step saves 2 and "
-                             "restores 2 blocks of the same shape"},
+                             "restores 2 blocks of the same shape (GB/s does not depend on "
+                             "the batch on the host)"},
           "cpu_baseline": {"value": value, "unit": "GB/s", "cores": samples[0]["cores"],
-                           "kind": "port", "sample": samples[0]["sample"]},
+                           "kind": "port", "sample": samples[0]["sample"],
+                           "host": samples[0]["host"]},
           "tokens_per_s": statistics.mean(s["tokens_per_s"] for s in samples),
           "torch_ops_cpu": torch_ops_sample(w, per_step),
           "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
