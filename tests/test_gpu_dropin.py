@@ -217,9 +217,11 @@ def test_fp8_block_reuse_waits_for_the_read_not_the_drain(cuda):
     assert np.array_equal(bits_u16(entry.scale), want_s[0])
 
 
-def test_fp8_back_to_back_restores_match_oracle(cuda):
+@pytest.mark.parametrize("split", [True, False])
+def test_fp8_back_to_back_restores_match_oracle(cuda, split):
     """Per-block staged restores share two staging halves without a join per
-    call; a batched restore on the same stream then grows the staging."""
+    call; a batched restore on the same stream then grows the staging. Without
+    split streams, saves and restores also share one kernel stream and ring."""
     shape = (2, 3, 16, 256, 8, 128)
     engine = FakeEngine(finite_pool(shape, cuda, seed=6))
     m = engine.manager
@@ -227,7 +229,7 @@ def test_fp8_back_to_back_restores_match_oracle(cuda):
     keys = [m.publish(b) for b in sources]
     pool = engine.pool
     source = bits_u16(pool)
-    cache = engine.create_cpu_prefix_cache(8 * per_block(pool), fp8=True, split_streams=True)
+    cache = engine.create_cpu_prefix_cache(8 * per_block(pool), fp8=True, split_streams=split)
     assert all(cache.save_block(k) for k in keys)
     entries = [cache._entries[k] for k in keys]
     want_p, want_s = oracle.fp8_save_blocks(source, sources)
@@ -240,11 +242,20 @@ def test_fp8_back_to_back_restores_match_oracle(cuda):
                 cache._copy_entry(e, b, wait=False)
         else:
             cache._copy_entries(entries, targets, wait=False)
+            # Saves interleaved with pending restores: a block being restored is
+            # saved again only after its restore has written it.
+            again = m.publish(targets[0])
+            assert cache.save_block(again)
         for b in targets:
             cache.before_block_use(b)
         oracle.fp8_restore_blocks(expected, targets, want_p, want_s)
         assert np.array_equal(bits_u16(pool), expected)
     cache.synchronize()
+    # The block saved right after its restore holds the restored values, whose
+    # FP8 slot is the original slot again (restore -> save is idempotent).
+    entry = cache._entries[again]
+    assert np.array_equal(entry.kv.view(torch.uint8).numpy(), want_p[0])
+    assert np.array_equal(bits_u16(entry.scale), want_s[0])
 
 
 def test_injected_failures_roll_back_and_retry_is_byte_exact(cuda):
