@@ -22,7 +22,7 @@
  * Inf / Inf is the default NaN with the sign set; an e4m3 NaN is 0x7F with the
  * input's sign bit. Dequantized NaN values are 0x7FFF (see dequantize_row).
  *
- * Build: oracle/build.py (gcc -O2 -fopenmp -fno-fast-math -ffp-contract=off).
+ * Build: oracle/build.py (gcc -O3 -mavx2 -fopenmp -fno-fast-math -ffp-contract=off).
  */
 #include <fenv.h>
 #include <math.h>
