@@ -469,6 +469,33 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
     return out
 
 
+def bf16_kernel_rates(torch, ops, w: Workload, pool, ids, hbm_peak: float, kernel_alone,
+                      stream) -> dict:
+    """The BF16 passthrough copy kernels on device memory: up to 64 blocks
+    gathered from the pool into dense device slots (save) and scattered back
+    (restore). Algorithmic HBM bytes: each block read once and written once
+    (2 x 37.7 MB per config-2 block). The TMA bulk-copy kernel and the SM
+    vector-copy kernel are ours; the copy engine (one cudaMemcpy2DAsync per
+    block) is listed beside them.
+    """
+    n = min(64, len(ids))
+    ids = ids[:n]
+    slots = torch.empty((n, w.bf16_block), dtype=torch.uint8, device=pool.device)
+    ptrs = [slots[i].data_ptr() for i in range(n)]
+    nbytes = 2 * n * w.bf16_block
+    out = {"blocks_per_launch": n, "bytes_per_launch": nbytes, "peak": hbm_peak}
+    for name, code in (("tma_copy_kernel", ops.COPY_TMA), ("sm_copy_kernel", ops.COPY_SM),
+                       ("copy_engine", ops.COPY_ENGINE)):
+        for direction, restore in (("save", False), ("restore", True)):
+            ms = kernel_alone(lambda code=code, restore=restore: ops.copy_blocks(
+                pool, ids, ptrs, restore=restore, method=code, stream=stream), stream)
+            achieved = nbytes / (ms / 1e3) / 1e9
+            out[f"{name}_{direction}"] = {"launch_ms": ms, "achieved": achieved,
+                                          "frac": achieved / hbm_peak}
+    del slots
+    return out
+
+
 def handoff_bench(torch, w: Workload, pool, args) -> dict:
     """KV handoff of one sequence (nanovllm/engine/kv_handoff.py:34-135): export
     its written tokens from 32 random pool blocks into a dense host snapshot
@@ -789,6 +816,10 @@ def run_ours(args) -> None:
                                    "frac": restore_achieved / hbm_peak,
                                    "launch_ms": restore_launch_ms}}
 
+    # ---- BF16 passthrough kernels, device-resident (pool <-> device slots) ----
+    bf16_kernels = bf16_kernel_rates(torch, ops, w, pool, save_ids, hbm_peak, kernel_alone,
+                                     save_stream) if single else None
+
     # ---- end to end through the C ABI with pinned host slots -----------------
     def e2e_fns(batch, save_mode, restore_mode):
         sids, rids = save_ids[:batch], restore_ids[:batch]
@@ -975,6 +1006,7 @@ def run_ours(args) -> None:
                 "pcie_frac_of_memcpy_h2d": pcie_per_dir / ceiling["h2d"],
                 "pcie_frac_of_memcpy_duplex": 2 * pcie_per_dir / ceiling["duplex_total"]},
         "roofline": roofline,
+        "bf16_kernels": bf16_kernels,
         "cpu_baseline": cpu,
         "clocks": clocks_e2e.summary() or clocks_dev.summary(),
         # kvoff kernels launched inside the two timed regions (device step: one

@@ -378,8 +378,7 @@ int launch(const Args& a, void* const* payload, void* const* scale, int32_t max_
     }
     if (lanes != 0) {
       const int64_t units = (int64_t)n * a.g.num_chunks * a.g.tiles_per_chunk;
-      const int64_t cap = max_ctas > 0 ? max_ctas : 0x7FFFFFFF;  // grid.x limit; kernels stride
-      const int64_t grid = units < cap ? units : cap;
+      const int64_t grid = streaming_grid(units, 1, max_ctas);
       if (kSave) {
         switch (lanes) {
           case 2: fp8_save_kernel<2><<<grid, kThreads, 0, stream>>>((const uint16_t*)a.pool, a.g, t, units); break;

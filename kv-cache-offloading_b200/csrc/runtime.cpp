@@ -101,6 +101,13 @@ int64_t grid_for(int64_t units, const void* kernel, int threads, size_t smem, in
   return grid < 1 ? 1 : grid;
 }
 
+int64_t streaming_grid(int64_t units, int64_t per_cta, int32_t max_ctas) {
+  int64_t grid = (units + per_cta - 1) / per_cta;
+  const int64_t cap = max_ctas > 0 ? max_ctas : 0x7FFFFFFF;
+  if (grid > cap) grid = cap;
+  return grid < 1 ? 1 : grid;
+}
+
 }  // namespace kvoff
 
 using namespace kvoff;

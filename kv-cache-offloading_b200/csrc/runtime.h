@@ -33,6 +33,12 @@ int ctas_per_sm(const void* kernel, int threads, size_t smem);
 // further capped by max_ctas when it is positive.
 int64_t grid_for(int64_t units, const void* kernel, int threads, size_t smem, int32_t max_ctas);
 
+// Grid size for a streaming kernel that strides over `units`: one CTA per
+// `per_cta` units, capped by max_ctas when it is positive and by the grid.x
+// limit. On B200 such an oversubscribed grid of short-lived CTAs keeps HBM
+// busier than a persistent grid of resident CTAs.
+int64_t streaming_grid(int64_t units, int64_t per_cta, int32_t max_ctas);
+
 }  // namespace kvoff
 
 #define KVOFF_TRY(expr)              \
