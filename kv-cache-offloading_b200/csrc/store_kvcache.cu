@@ -4,12 +4,12 @@
 // Token i's K row (row_bytes, at key + i * key_stride_bytes) goes to
 // k_cache + slot * row_bytes, and likewise for V; slot = slot_mapping[i],
 // and -1 marks a padded token that is skipped. The copy is a pure byte move,
-// so any cache dtype is moved bit-exactly. CTAs of 128 threads stride over the
-// tokens; the K and V rows move with the widest unit (16, 8, 4, 2 or 1
-// bytes) that every address and stride allows. Offsets are 64-bit. A CTA
-// iteration covers kTokens tokens: their slots are loaded first, then every
-// thread issues all of its K and V loads before the stores, so each thread
-// keeps 2 * kTokens independent loads in flight.
+// so any cache dtype is moved bit-exactly. One warp moves one row: row r is
+// token r / 2, its K row for even r and its V row for odd r. Each lane issues
+// its row loads (the widest unit, 16, 8, 4, 2 or 1 bytes, that every address
+// and stride allows) without waiting for the slot, and only the stores wait
+// for it. The grid has one CTA per kWarps rows, so a prefill of a few
+// thousand tokens has all of its rows in flight at once. Offsets are 64-bit.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -18,8 +18,9 @@
 namespace kvoff {
 namespace {
 
-constexpr int kThreads = 128;
-constexpr int kTokens = 4;  // tokens per CTA iteration: 8 independent loads per thread
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kPerLane = 4;  // loads per lane per pass: a warp moves 32 * kPerLane vectors
 
 template <typename V>
 __global__ void __launch_bounds__(kThreads)
@@ -29,35 +30,33 @@ __global__ void __launch_bounds__(kThreads)
                          int64_t row_bytes, const int32_t* __restrict__ slot_mapping,
                          int64_t num_tokens, int64_t num_slots, int32_t* bad_slots) {
   const int64_t vecs = row_bytes / (int64_t)sizeof(V);
-  for (int64_t first = (int64_t)blockIdx.x * kTokens; first < num_tokens;
-       first += (int64_t)gridDim.x * kTokens) {
-    int64_t slot[kTokens];
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = 2 * num_tokens;
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows;
+       r += (int64_t)gridDim.x * kWarps) {
+    const int64_t token = r >> 1;
+    const bool is_v = (r & 1) != 0;
+    const V* src = reinterpret_cast<const V*>(is_v ? value + token * value_stride
+                                                   : key + token * key_stride);
+    const int64_t slot = (int64_t)__ldg(slot_mapping + token);
+    for (int64_t base = 0; base < vecs; base += 32 * kPerLane) {
+      V v[kPerLane];
 #pragma unroll
-    for (int t = 0; t < kTokens; ++t) {
-      const int64_t i = first + t;
-      slot[t] = i < num_tokens ? (int64_t)__ldg(slot_mapping + i) : -1;
-      if (slot[t] >= num_slots) {  // out of range: skipped, counted once per token
-        if (threadIdx.x == 0 && bad_slots != nullptr) atomicAdd(bad_slots, 1);
-        slot[t] = -1;
+      for (int k = 0; k < kPerLane; ++k) {
+        const int64_t j = base + k * 32 + lane;
+        if (j < vecs) v[k] = __ldg(src + j);
       }
-    }
-    for (int64_t j = threadIdx.x; j < vecs; j += kThreads) {
-      V k[kTokens], v[kTokens];
+      if (slot >= 0 && slot < num_slots) {
+        V* dst = reinterpret_cast<V*>((is_v ? v_cache : k_cache) + slot * row_bytes);
 #pragma unroll
-      for (int t = 0; t < kTokens; ++t) {
-        if (slot[t] >= 0) {
-          k[t] = __ldg(reinterpret_cast<const V*>(key + (first + t) * key_stride) + j);
-          v[t] = __ldg(reinterpret_cast<const V*>(value + (first + t) * value_stride) + j);
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < kTokens; ++t) {
-        if (slot[t] >= 0) {
-          reinterpret_cast<V*>(k_cache + slot[t] * row_bytes)[j] = k[t];
-          reinterpret_cast<V*>(v_cache + slot[t] * row_bytes)[j] = v[t];
+        for (int k = 0; k < kPerLane; ++k) {
+          const int64_t j = base + k * 32 + lane;
+          if (j < vecs) dst[j] = v[k];
         }
       }
     }
+    if (!is_v && lane == 0 && slot >= num_slots && bad_slots != nullptr)
+      atomicAdd(bad_slots, 1);  // out of range: skipped, counted once per token
   }
 }
 
@@ -65,8 +64,7 @@ template <typename V>
 int launch(const void* key, int64_t ks, const void* value, int64_t vs, void* kc, void* vc,
            int64_t row_bytes, const int32_t* slots, int64_t n, int64_t num_slots, int32_t* bad,
            cudaStream_t stream) {
-  const void* kernel = (const void*)store_kvcache_kernel<V>;
-  const int64_t grid = grid_for((n + kTokens - 1) / kTokens, kernel, kThreads, 0, 0);
+  const int64_t grid = streaming_grid(2 * n, kWarps, 0);
   store_kvcache_kernel<V><<<grid, kThreads, 0, stream>>>(
       static_cast<const uint8_t*>(key), ks, static_cast<const uint8_t*>(value), vs,
       static_cast<uint8_t*>(kc), static_cast<uint8_t*>(vc), row_bytes, slots, n, num_slots, bad);
