@@ -8,8 +8,8 @@
 // token r / 2, its K row for even r and its V row for odd r. Each lane issues
 // its row loads (the widest unit, 16, 8, 4, 2 or 1 bytes, that every address
 // and stride allows) without waiting for the slot, and only the stores wait
-// for it. The grid has one CTA per kWarps rows, so a prefill of a few
-// thousand tokens has all of its rows in flight at once. Offsets are 64-bit.
+// for it. The grid has one CTA per kWarps rows, so the rows of a prefill of a
+// few thousand tokens are in flight in one or two waves. Offsets are 64-bit.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
