@@ -16,19 +16,22 @@ small fixtures that pin the CPU oracle and, through it, the CUDA library:
                      SHA-256 digests of the 16 saved FP8 slots (payload and
                      scales) and of the 16 restored blocks, plus the BF16
                      round trip, produced by the reference CPUBlockCache.
-* store_kvcache.json - attention.store_kvcache restated as torch indexing
-                     (nanovllm/layers/attention.py:10-40; its Triton kernel
-                     needs a GPU, so this fixture pins the restatement only):
-                     digests of the caches after the scatter of seeded inputs.
+* store_kvcache.json - the reference's own store_kvcache
+                     (nanovllm/layers/attention.py:10-40): its Triton kernel
+                     runs on CPU tensors under Triton's interpreter
+                     (TRITON_INTERPRET=1), on seeded inputs; digests of the
+                     caches after the scatter. The torch-indexing restatement
+                     must produce the same bytes.
 
-The reference checkout is located by KVOFF_REFERENCE (default: the mount the
-build container provides). Run from the repository root:
+The reference checkout is located by KVOFF_REFERENCE (default: a "reference"
+directory beside this repository). Run from the repository root:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [--only store_kvcache ...]
 """
 
 from __future__ import annotations
 
+import argparse
 import hashlib
 import importlib.util
 import json
@@ -38,8 +41,12 @@ from collections import deque
 from pathlib import Path
 from types import ModuleType, SimpleNamespace
 
-import numpy as np
-import torch
+# The reference's store_kvcache is a Triton kernel; the interpreter runs it on
+# CPU tensors. The variable is read when the kernel's module is imported.
+os.environ["TRITON_INTERPRET"] = "1"
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent))
@@ -185,7 +192,21 @@ def config1(bm_mod, cache_mod) -> dict:
     return result
 
 
+def reference_store_kvcache():
+    """store_kvcache of the reference (nanovllm/layers/attention.py:10-40)."""
+    if "nanovllm" not in sys.modules:
+        package = ModuleType("nanovllm")
+        package.__path__ = [str(ENGINE_ROOT)]
+        sys.modules["nanovllm"] = package
+    spec = importlib.util.spec_from_file_location("nanovllm.layers.attention",
+                                                  ENGINE_ROOT / "layers" / "attention.py")
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module.store_kvcache
+
+
 def store_kvcache_fixture() -> dict:
+    store = reference_store_kvcache()
     out = {}
     for name, (n, h, d, nb, bs, pad) in workloads.STORE_CASES.items():
         qkv, slots, k_in, v_in = workloads.store_kvcache_inputs(name)
@@ -193,24 +214,42 @@ def store_kvcache_fixture() -> dict:
         k = rows[:, pad:pad + h * d].view(n, h, d)
         v = rows[:, pad + h * d:].view(n, h, d)
         k_cache, v_cache = bf16(k_in.copy()), bf16(v_in.copy())
+        store(k, v, k_cache, v_cache, torch.from_numpy(slots))  # the reference kernel
+        # The restatement the oracle follows must give the same bytes.
+        k_check, v_check = bf16(k_in.copy()), bf16(v_in.copy())
         m = torch.from_numpy(slots) != -1
         idx = torch.from_numpy(slots.astype(np.int64))[m]
-        k_cache.view(-1, h * d)[idx] = k.reshape(n, -1)[m]
-        v_cache.view(-1, h * d)[idx] = v.reshape(n, -1)[m]
+        k_check.view(-1, h * d)[idx] = k.reshape(n, -1)[m]
+        v_check.view(-1, h * d)[idx] = v.reshape(n, -1)[m]
+        assert np.array_equal(bits(k_cache), bits(k_check)), name
+        assert np.array_equal(bits(v_cache), bits(v_check)), name
         out[name] = {"k_cache_sha256": digest(bits(k_cache)),
-                     "v_cache_sha256": digest(bits(v_cache))}
+                     "v_cache_sha256": digest(bits(v_cache)),
+                     "source": "reference Triton store_kvcache_kernel under TRITON_INTERPRET=1"}
     return out
 
 
+FIXTURES = ("fp8_rows", "dropin_tiny", "store_kvcache", "config1")
+
+
 def main():
+    parser = argparse.ArgumentParser(description=__doc__,
+                                     formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--only", nargs="+", choices=FIXTURES, default=list(FIXTURES))
+    only = set(parser.parse_args().only)
     if not ENGINE_ROOT.exists():
         raise SystemExit(f"reference checkout not found at {REFERENCE}")
     torch.manual_seed(0)
     bm_mod, cache_mod = load_reference_engine()
-    np.savez_compressed(HERE / "fp8_rows.npz", **fp8_rows(cache_mod))
-    np.savez_compressed(HERE / "dropin_tiny.npz", **dropin_tiny(bm_mod, cache_mod))
-    (HERE / "store_kvcache.json").write_text(json.dumps(store_kvcache_fixture(), indent=1) + "\n")
-    (HERE / "config1.json").write_text(json.dumps(config1(bm_mod, cache_mod), indent=1) + "\n")
+    if "fp8_rows" in only:
+        np.savez_compressed(HERE / "fp8_rows.npz", **fp8_rows(cache_mod))
+    if "dropin_tiny" in only:
+        np.savez_compressed(HERE / "dropin_tiny.npz", **dropin_tiny(bm_mod, cache_mod))
+    if "store_kvcache" in only:
+        (HERE / "store_kvcache.json").write_text(
+            json.dumps(store_kvcache_fixture(), indent=1) + "\n")
+    if "config1" in only:
+        (HERE / "config1.json").write_text(json.dumps(config1(bm_mod, cache_mod), indent=1) + "\n")
     meta = {"torch": torch.__version__, "numpy": np.__version__,
             "threads": torch.get_num_threads()}
     (HERE / "generated_with.json").write_text(json.dumps(meta, indent=1) + "\n")

@@ -111,7 +111,9 @@ def special_rows(head_dim: int, seed: int) -> np.ndarray:
 
 
 # store_kvcache cases: (tokens, KV heads, head_dim, blocks, block_size, qkv row padding).
-STORE_CASES = {"vec": (300, 8, 128, 6, 64, 3 * 1024), "tiny": (37, 1, 4, 3, 16, 5)}
+# name: (tokens, KV heads, head dim, cache blocks, block size, q width before K in each qkv row)
+STORE_CASES = {"vec": (300, 8, 128, 6, 64, 3 * 1024), "tiny": (37, 1, 4, 3, 16, 5),
+               "prefill": (4096, 8, 128, 20, 256, 32 * 128)}
 
 
 def store_kvcache_inputs(name: str):
