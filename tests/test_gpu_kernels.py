@@ -85,6 +85,44 @@ def test_fp8_save_restore_bit_exact(cuda, d, heads, block_size):
     assert np.array_equal(u16(pool), bits)
 
 
+def test_kernels_match_the_reference_quantizer_run_on_the_gpu(cuda):
+    """The reference's fp8_quantize / fp8_dequantize torch ops (kept verbatim in
+    the drop-in module) run on the same CUDA tensors, as the reference engine
+    runs them. Every row with finite values is bit-identical. Rows holding Inf
+    or NaN follow the CPU reference's encodings in the kernels, and ATen's CUDA
+    ops differ from those only in NaN sign bits, so NaN-ness is compared there."""
+    from kvoff import ops
+    from kvoff.cpu_prefix_cache import fp8_dequantize, fp8_quantize
+
+    bits = special_pool(2, 4, 256, 8, 128, seed=5)
+    pool = to_bf16(bits, cuda)
+    g = ops.geometry(pool)
+    ids, targets = [0, 2], [1, 3]
+    payload, scale = empty_slots(2, g, cuda)
+    ops.save_fp8(pool, ids, [p.data_ptr() for p in payload], [s.data_ptr() for s in scale])
+    slot_shape = (2, pool.shape[1], *pool.shape[3:])
+    scale_shape = (*slot_shape[:-1], 1)
+    finite = ((bits & 0x7F80) != 0x7F80).all(-1)  # [2, L, NB, BS, H]
+    for i, b in enumerate(ids):
+        ref_p = torch.empty(slot_shape, dtype=torch.float8_e4m3fn, device=cuda)
+        ref_s = torch.empty(scale_shape, dtype=torch.bfloat16, device=cuda)
+        fp8_quantize(pool[:, :, b], ref_p, ref_s)
+        ok = finite[:, :, b]
+        got_p, want_p = u8(payload[i]).reshape(slot_shape), u8(ref_p)
+        got_s, want_s = u16(scale[i].view(torch.bfloat16)).reshape(scale_shape), u16(ref_s)
+        assert np.array_equal(got_p[ok], want_p[ok])
+        assert np.array_equal(got_s[ok], want_s[ok])
+        nan8 = lambda a: (a & 0x7F) == 0x7F  # noqa: E731
+        assert np.array_equal(nan8(got_p[~ok]), nan8(want_p[~ok]))
+        # Dequantize this slot with both and compare the finite rows.
+        ref_out = torch.empty(slot_shape, dtype=torch.bfloat16, device=cuda)
+        fp8_dequantize(payload[i].view(torch.float8_e4m3fn).view(slot_shape),
+                       scale[i].view(torch.bfloat16).view(scale_shape), ref_out)
+        ops.restore_fp8(pool, [targets[i]], [payload[i].data_ptr()], [scale[i].data_ptr()])
+        got = u16(pool[:, :, targets[i]])
+        assert np.array_equal(got[ok], u16(ref_out)[ok])
+
+
 def test_fp8_restore_of_arbitrary_slot_bits(cuda):
     from kvoff import ops
 
