@@ -6,11 +6,12 @@ fork) on one GPU, from a checkout of the reference given by `--reference`
 (default `baseline/_ref`, a copy of the reference's `bench/` and
 `nanovllm_upstream/` trees; it is not part of this repository). Two arms:
 
-* `--impl kvoff`: the engine with kvoff's drop-ins put in place exactly as the
+* `--impl kvoff`: the engine with kvoff's drop-ins put in place as the
   integration guide describes: `nanovllm/engine/cpu_prefix_cache.py` and
-  `nanovllm/engine/kv_handoff.py` replaced by kvoff's modules, and
-  `store_kvcache` in `nanovllm/layers/attention.py` bound to
-  `kvoff.attention.store_kvcache`.
+  `nanovllm/engine/kv_handoff.py` replaced by kvoff's modules,
+  `nanovllm/layers/attention.py` importing `kvoff.attention.store_kvcache` over
+  its Triton one, and the runner's `kvoff_tier` method (used only under tensor
+  parallelism) added to `ModelRunner`.
 * `--impl reference`: the stock engine (torch-op FP8 quantizer on the copy
   streams, the Triton `store_kvcache_kernel`).
 
@@ -51,6 +52,20 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 KVOFF_DIR = ROOT / "kv-cache-offloading_b200"
 DROPINS = ("cpu_prefix_cache.py", "kv_handoff.py")
+# The one method tensor parallelism needs on the engine's runner (every rank).
+RUNNER_METHOD = """
+
+def _kvoff_tier(self, op, *args):
+    from kvoff.tp_tier import dispatch
+    return dispatch(self, op, *args)
+
+
+ModelRunner.kvoff_tier = _kvoff_tier
+"""
+STORE_DROPIN = """
+
+from kvoff.attention import store_kvcache  # noqa: E402,F811  (kvoff's slot store)
+"""
 
 # Qwen3-8B architecture (the public model configuration's hyperparameters).
 QWEN3_8B = {
@@ -122,28 +137,40 @@ def _engine_tree(reference: Path, impl: str, scratch: Path) -> Path:
         engine = tree / "nanovllm_upstream" / "nanovllm" / "engine"
         for name in DROPINS:
             shutil.copyfile(KVOFF_DIR / "kvoff" / name, engine / name)
+        with open(engine / "model_runner.py", "a") as runner:
+            runner.write(RUNNER_METHOD)
+        # Rebinds the module's store_kvcache, which Attention.forward calls, in every
+        # process that imports it (tensor-parallel ranks included).
+        with open(engine.parent / "layers" / "attention.py", "a") as attention:
+            attention.write(STORE_DROPIN)
     return tree
 
 
-def _install(tree: Path, impl: str) -> None:
-    """Import the engine from the tree and bind the model-free stand-ins (and kvoff's store)."""
+def _install(tree: Path, impl: str, random_weights: bool = True,
+             eos_token_id: int = QWEN3_8B["eos_token_id"]) -> None:
+    """Import the engine from the tree and bind the model-free stand-ins (and kvoff's store).
+
+    random_weights=False keeps the engine's own loader, for a model directory
+    that holds a checkpoint (tensor-parallel ranks load it in their own
+    processes, where a stand-in bound here would not reach).
+    """
     sys.path[:0] = [str(tree), str(tree / "nanovllm_upstream"), str(KVOFF_DIR)]
     import transformers
 
     import nanovllm.engine.model_runner as model_runner
     import nanovllm.layers.attention as attention
 
-    model_runner.load_model = _random_init
+    if random_weights:
+        model_runner.load_model = _random_init
     transformers.AutoTokenizer.from_pretrained = staticmethod(
-        lambda *args, **kwargs: _IdTokenizer(QWEN3_8B["eos_token_id"]))
+        lambda *args, **kwargs: _IdTokenizer(eos_token_id))
     if impl == "kvoff":
-        from kvoff.attention import store_kvcache
-
-        attention.store_kvcache = store_kvcache
         import nanovllm.engine.cpu_prefix_cache as cache
 
-        if not hasattr(cache.CPUBlockCache, "save_blocks"):
-            raise RuntimeError("the engine tree did not pick up kvoff's cpu_prefix_cache")
+        if not (hasattr(cache.CPUBlockCache, "save_blocks")
+                and attention.store_kvcache.__module__ == "kvoff.attention"
+                and callable(getattr(model_runner.ModelRunner, "kvoff_tier", None))):
+            raise RuntimeError("the engine tree did not pick up kvoff's drop-ins")
 
 
 def main() -> int:

@@ -2,7 +2,8 @@
 
 The agent-replay measurement (trajectories/min) runs the reference's own
 harness and engine; its kvoff arm must actually use kvoff's CPU tier, KV
-handoff and store_kvcache, and its reference arm must not. Checked on CPU in a
+handoff, store_kvcache and the runner's tensor-parallel tier method, and its
+reference arm must not. Checked on CPU in a
 child process (the engine's modules are imported there, not here), without
 running a model. Skipped when no reference checkout is available.
 """
@@ -38,6 +39,7 @@ print(json.dumps({{
     "handoff": sys.modules["nanovllm.engine.kv_handoff"].__file__,
     "cache": sys.modules["nanovllm.engine.cpu_prefix_cache"].__file__,
     "loader": model_runner.load_model.__name__,
+    "runner_tier": callable(getattr(model_runner.ModelRunner, "kvoff_tier", None)),
     "eos": transformers.AutoTokenizer.from_pretrained("unused").eos_token_id,
     "tree": str(tree),
 }}))
@@ -63,7 +65,7 @@ def test_replay_arms_bind_the_expected_modules(impl, tmp_path):
     assert same_handoff == same_cache == (impl == "kvoff")
     if impl == "kvoff":
         assert got["store"] == "kvoff.attention"
-        assert got["cache_has_batched_calls"]
+        assert got["cache_has_batched_calls"] and got["runner_tier"]
     else:
         assert got["store"] == "nanovllm.layers.attention"
-        assert not got["cache_has_batched_calls"]
+        assert not (got["cache_has_batched_calls"] or got["runner_tier"])
