@@ -84,6 +84,16 @@ CPU_TIER = ["--policy", "cpu_backed", "--cpu-cache-save-on-release", "--cpu-cach
             "--cpu-cache-split-streams", "--cpu-cache-fp8", "--cpu-cache-hybrid",
             "--cuda-graphs", "--ignore-eos", "--gpu-memory-utilization", "0.9"]
 
+
+
+def tier_flags(tier: str) -> list[str]:
+    """Harness flags for an FP8 or BF16 CPU tier, or for the GPU-only policy."""
+    if tier == "none":
+        return ["--policy", "gpu_only", "--cuda-graphs", "--ignore-eos",
+                "--gpu-memory-utilization", "0.9"]
+    return [flag for flag in CPU_TIER if tier == "fp8" or flag != "--cpu-cache-fp8"]
+
+
 WORKLOADS = {
     "config3": ["--num-agents", "4", "--turns-per-agent", "3", "--initial-prompt", "32768",
                 "--tool-result-tokens", "2048", "--output-tokens", "256", "--tool-wait-s", "5",
@@ -183,7 +193,11 @@ def main() -> int:
                         help="checkout holding the reference's bench/ and nanovllm_upstream/")
     parser.add_argument("--out", type=Path, default=None,
                         help="directory for the harness's result.json and trace.json")
+    parser.add_argument("--tier", choices=("fp8", "bf16", "none"), default="fp8",
+                        help="CPU tier payload; none runs the harness's GPU-only policy "
+                             "(no CPU tier, so --impl makes no difference to the copy path)")
     args = parser.parse_args()
+    flags = tier_flags(args.tier) + WORKLOADS[args.workload]
 
     reference = args.reference.resolve()
     if not (reference / "bench" / "agent_replay.py").is_file():
@@ -207,7 +221,7 @@ def main() -> int:
         from bench import agent_replay
 
         sys.argv = ["agent_replay", "--model", str(model), "--out", str(out),
-                    "--seed", str(args.seed), *CPU_TIER, *WORKLOADS[args.workload]]
+                    "--seed", str(args.seed), *flags]
         started = time.perf_counter()
         agent_replay.main()
         wall = time.perf_counter() - started
@@ -218,10 +232,10 @@ def main() -> int:
     print(json.dumps({
         "metric": "completed agent trajectories per minute", "unit": "traj/min",
         "value": summary["completed_trajectories_per_min"], "higher_is_better": True,
-        "impl": args.impl, "workload": args.workload, "seed": args.seed,
+        "impl": args.impl, "workload": args.workload, "tier": args.tier, "seed": args.seed,
         "data": "synthetic (harness-seeded uniform token ids, random-init weights)",
         "gpu": torch.cuda.get_device_name(0), "process_wall_s": wall,
-        "flags": [*CPU_TIER, *WORKLOADS[args.workload]], "summary": summary,
+        "flags": flags, "summary": summary,
     }))
     return 0
 

@@ -88,8 +88,12 @@ class _FollowerManager:
 # BF16: "engine" (one strided DMA per block), "tma" (cp.async.bulk gather into
 # device staging + DMA) or "sm" (vector-copy kernel over PCIe). Override with
 # KVOFF_FP8_SAVE / KVOFF_FP8_RESTORE / KVOFF_BF16_SAVE / KVOFF_BF16_RESTORE.
+# BF16 restores default to "tma": a strided (2D) DMA into the pool holds up the
+# compute stream's own small host-to-device copies queued behind it, so a
+# prefill that overlaps a run of restores stalls until they drain; a plain
+# DMA into staging plus the scatter kernel lets it run alongside.
 DEFAULT_MODES = {"fp8_save": "staged", "fp8_restore": "staged",
-                 "bf16_save": "engine", "bf16_restore": "engine"}
+                 "bf16_save": "engine", "bf16_restore": "tma"}
 _MODE_CHOICES = {"fp8_save": ("staged", "mapped"), "fp8_restore": ("staged", "mapped"),
                  "bf16_save": ("engine", "tma", "sm"), "bf16_restore": ("engine", "tma", "sm")}
 
