@@ -863,6 +863,13 @@ def run_ours(args) -> None:
                     ops.copy_blocks(pool, rids[k:k + n], [x.data_ptr() for x in st_r[:n]],
                                     restore=True, method=ops.COPY_TMA, stream=restore_stream)
             return save, restore
+        if method == "staged":
+            sp, rp = [x.data_ptr() for x in ss], [x.data_ptr() for x in rs]
+            save = lambda: ops.copy_blocks_staged(  # noqa: E731
+                pool, sids, sp, bf16_staging["save"], stream=save_stream)
+            restore = lambda: ops.copy_blocks_staged(  # noqa: E731
+                pool, rids, rp, bf16_staging["restore"], restore=True, stream=restore_stream)
+            return save, restore
         code = ops.COPY_SM if method == "sm" else ops.COPY_ENGINE
         sp = [slab.device_alias(x) if method == "sm" else x.data_ptr() for x in ss]
         rp = [slab.device_alias(x) if method == "sm" else x.data_ptr() for x in rs]
@@ -889,7 +896,7 @@ def run_ours(args) -> None:
             save, restore = e2e_fns(batch, save_m, restore_m)
             row[f"fp8_save_{save_m}_restore_{restore_m}"] = {
                 "duplex": rate(concurrent(save, restore), batch, 2, **few)}
-        for method in ("engine", "tma", "sm"):
+        for method in ("staged", "engine", "tma", "sm"):
             save, restore = bf16_fns(batch, method)
             row[f"bf16_{method}"] = {
                 "save": rate(concurrent(save, lambda: None), batch, 1, **few),

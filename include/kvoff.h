@@ -221,6 +221,20 @@ KVOFF_API int kvoff_fp8_restore_blocks_staged_ev(void* pool, int64_t num_chunks,
 KVOFF_API int kvoff_stream_join_pipeline(void* stream);
 
 /*
+ * Yield mode for the staged calls on `stream` (FP8 and BF16; off by default).
+ * With it on, each group's host copy on `stream` starts only after the
+ * previous group's kernel has finished (restore), and each group's kernel
+ * only after the previous group's host copy (save). The copy engine then goes
+ * idle for one kernel's duration between groups, so small copies that other
+ * streams queue on it meanwhile (a compute stream's per-step inputs and
+ * sampled tokens) run there instead of waiting behind a whole run of block
+ * transfers. It costs a few percent of a long run's throughput. The
+ * reference's restores and saves leave the same gaps, because their copies
+ * and kernels share one stream (cpu_prefix_cache.py:236-243, :311-322).
+ */
+KVOFF_API int kvoff_stream_set_yield(void* stream, int32_t enable);
+
+/*
  * Byte-exact block passthrough (BF16 mode): move whole blocks between the
  * pool and dense slots. Strides and sizes are in BYTES here. direction
  * KVOFF_SAVE copies pool -> slots[i], KVOFF_RESTORE slots[i] -> pool.
@@ -233,6 +247,35 @@ KVOFF_API int kvoff_copy_blocks(void* pool, int64_t num_chunks, int64_t chunk_st
                                 int64_t chunk_bytes, const int64_t* block_ids, int64_t count,
                                 void* const* slots, int32_t direction, int32_t method,
                                 int32_t max_ctas, void* stream);
+
+/*
+ * Staged byte-exact block passthrough between the pool and pinned host slots,
+ * pipelined like the staged FP8 calls. TMA bulk-copy kernels (the SM copy
+ * kernel where an address or stride is not 16-byte aligned) gather blocks
+ * into, or scatter them out of, one half of the device staging buffer
+ * (staging_blocks dense blocks of num_chunks * chunk_bytes) on a library-owned
+ * kernel stream, while plain DMA moves the other half over PCIe on `stream`.
+ * Every DMA is a contiguous copy: a strided DMA straight into the pool holds
+ * up later small copies queued behind it, stalling the compute stream's
+ * inputs while restores run. Same bytes as kvoff_copy_blocks.
+ *   KVOFF_SAVE: the gather kernels wait for wait_events (none: for earlier work
+ *     on `stream`); `event`, when non-null, is recorded once every pool block
+ *     has been read, so a block's next writer need not wait for the drain.
+ *   KVOFF_RESTORE: `event`, when non-null, is recorded after the last pool
+ *     write and `stream` is not joined; without it `stream` waits for the
+ *     kernels. wait_events must be empty.
+ * kvoff_stream_join_pipeline(stream) makes `stream` wait for the kernels.
+ * Replaces payload.copy_(source) (cpu_prefix_cache.py:319) and
+ * target.copy_(entry.kv) (:386) in BF16 mode.
+ */
+KVOFF_API int kvoff_copy_blocks_staged(void* pool, int64_t num_chunks,
+                                       int64_t chunk_stride_bytes, int64_t block_stride_bytes,
+                                       int64_t num_blocks, int64_t chunk_bytes,
+                                       const int64_t* block_ids, int64_t count,
+                                       void* const* host_slots, void* staging,
+                                       int64_t staging_blocks, int32_t direction,
+                                       void* const* wait_events, int32_t num_wait_events,
+                                       void* event, void* stream);
 
 /*
  * Token-range copy for KV handoff: the first num_tokens tokens of a sequence,

@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "runtime.h"
 
 namespace kvoff {
@@ -347,6 +349,120 @@ int kvoff_copy_blocks(void* pool, int64_t num_chunks, int64_t chunk_stride_bytes
   else
     KVOFF_TRY(copy_kernel(static_cast<uint8_t*>(pool), g, block_ids, count, slots, save, method,
                           max_ctas, s));
+  return ok();
+}
+
+int kvoff_copy_blocks_staged(void* pool, int64_t num_chunks, int64_t chunk_stride_bytes,
+                             int64_t block_stride_bytes, int64_t num_blocks, int64_t chunk_bytes,
+                             const int64_t* block_ids, int64_t count, void* const* host_slots,
+                             void* staging, int64_t staging_blocks, int32_t direction,
+                             void* const* wait_events, int32_t num_wait_events, void* event,
+                             void* stream) {
+  if (injected("copy_blocks_staged")) return KVOFF_EINJECTED;
+  if (count < 0) return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: negative count");
+  if (num_chunks <= 0 || chunk_bytes <= 0 || chunk_stride_bytes < 0 || block_stride_bytes < 0 ||
+      num_blocks <= 0)
+    return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: bad geometry");
+  if (direction != KVOFF_SAVE && direction != KVOFF_RESTORE)
+    return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: bad direction %d", direction);
+  if (num_wait_events < 0 || (num_wait_events > 0 && wait_events == nullptr) ||
+      (num_wait_events > 0 && direction != KVOFF_SAVE))
+    return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: bad wait event list");
+  if (count == 0) return ok();
+  if (pool == nullptr || block_ids == nullptr || host_slots == nullptr || staging == nullptr ||
+      staging_blocks <= 0)
+    return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: null pointer or no staging");
+  for (int64_t i = 0; i < count; ++i) {
+    if (block_ids[i] < 0 || block_ids[i] >= num_blocks)
+      return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: block id %lld out of range [0, %lld)",
+                  (long long)block_ids[i], (long long)num_blocks);
+    if (host_slots[i] == nullptr)
+      return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: null slot at %lld", (long long)i);
+  }
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, staging) != cudaSuccess ||
+      attr.type != cudaMemoryTypeDevice) {
+    cudaGetLastError();
+    return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: staging must be device memory");
+  }
+  const CopyGeometry g{num_chunks, chunk_stride_bytes, block_stride_bytes, chunk_bytes};
+  const int64_t bb = num_chunks * chunk_bytes;  // one dense block in staging and in a slot
+  // TMA where every address and stride allows 16-byte bulk copies, else the SM kernel.
+  const int method = aligned16(pool) && aligned16(staging) && chunk_stride_bytes % 16 == 0 &&
+                             block_stride_bytes % 16 == 0 && chunk_bytes % 16 == 0
+                         ? KVOFF_COPY_TMA
+                         : KVOFF_COPY_SM;
+  uint8_t* base = static_cast<uint8_t*>(pool);
+  uint8_t* stage = static_cast<uint8_t*>(staging);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool save = direction == KVOFF_SAVE;
+  const bool pipelined = staging_blocks >= 2;
+  const int64_t half = staging_blocks / 2;
+  const int64_t cap = pipelined ? half : staging_blocks;
+  const int64_t group = cap < kMaxBatch ? cap : kMaxBatch;
+  std::unique_lock<std::mutex> lock(pipe_mutex(), std::defer_lock);
+  Pipe* p = nullptr;
+  cudaStream_t ks = s;  // stream that runs the gather / scatter kernels
+  if (pipelined) {
+    lock.lock();
+    KVOFF_TRY(pipe_for(s, staging, &p));
+    ks = p->aux;
+  }
+  if (num_wait_events > 0) {  // a save's kernels need only these, not earlier DMA on `s`
+    for (int32_t i = 0; i < num_wait_events; ++i)
+      KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, static_cast<cudaEvent_t>(wait_events[i]), 0),
+                            "cudaStreamWaitEvent (wait event)"));
+  } else if (pipelined) {  // kernels follow the caller stream's earlier work
+    KVOFF_TRY(cuda_status(cudaEventRecord(p->start, s), "cudaEventRecord"));
+    KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, p->start, 0), "cudaStreamWaitEvent"));
+  }
+  void* dense[kMaxBatch];
+  for (int64_t first = 0; first < count; first += group) {
+    const int64_t n = (count - first) < group ? (count - first) : group;
+    const int h = pipelined ? p->next : 0;
+    for (int64_t i = 0; i < n; ++i) dense[i] = stage + (h * half + i) * bb;
+    if (save) {
+      if (pipelined)  // earlier copies out of this half are done (and, yielding, the other's)
+        KVOFF_TRY(pipe_wait_half(p, h, ks));
+      KVOFF_TRY(copy_kernel(base, g, block_ids + first, n, dense, true, method, 0, ks));
+      if (event != nullptr && first + n >= count)  // every pool block has been read
+        KVOFF_TRY(cuda_status(cudaEventRecord(static_cast<cudaEvent_t>(event), ks),
+                              "cudaEventRecord (source done)"));
+      if (pipelined) {
+        KVOFF_TRY(cuda_status(cudaEventRecord(p->ready[h], ks), "cudaEventRecord"));
+        KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p->ready[h], 0), "cudaStreamWaitEvent"));
+      }
+      KVOFF_TRY(copy_runs(host_slots + first, dense, n, bb, s, "staged block save copy"));
+      if (pipelined) {
+        KVOFF_TRY(cuda_status(cudaEventRecord(p->freed[h], s), "cudaEventRecord"));
+        p->freed_recorded[h] = true;
+        p->next = 1 - h;
+      }
+    } else {
+      if (pipelined)  // earlier kernels reading this half are done (and, yielding, the other's)
+        KVOFF_TRY(pipe_wait_half(p, h, s));
+      KVOFF_TRY(copy_runs(dense, host_slots + first, n, bb, s, "staged block restore copy"));
+      if (pipelined) {
+        KVOFF_TRY(cuda_status(cudaEventRecord(p->ready[h], s), "cudaEventRecord"));
+        KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, p->ready[h], 0), "cudaStreamWaitEvent"));
+      }
+      KVOFF_TRY(copy_kernel(base, g, block_ids + first, n, dense, false, method, 0, ks));
+      if (pipelined) {
+        KVOFF_TRY(cuda_status(cudaEventRecord(p->freed[h], ks), "cudaEventRecord"));
+        p->freed_recorded[h] = true;
+        p->next = 1 - h;
+      }
+    }
+  }
+  if (!save) {
+    if (event != nullptr) {  // the caller orders readers of the blocks on this event
+      KVOFF_TRY(cuda_status(cudaEventRecord(static_cast<cudaEvent_t>(event), ks),
+                            "cudaEventRecord (done)"));
+    } else if (pipelined) {  // the caller's stream sees every pool write of this call
+      KVOFF_TRY(cuda_status(cudaEventRecord(p->done, ks), "cudaEventRecord"));
+      KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p->done, 0), "cudaStreamWaitEvent"));
+    }
+  }
   return ok();
 }
 

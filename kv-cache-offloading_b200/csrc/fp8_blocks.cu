@@ -20,7 +20,6 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include <map>
 #include <mutex>
 
 #include "codec.cuh"
@@ -410,67 +409,6 @@ int launch(const Args& a, void* const* payload, void* const* scale, int32_t max_
 int64_t payload_bytes(const Geometry& g) { return g.num_chunks * g.rows_per_chunk * g.head_dim; }
 int64_t scale_bytes(const Geometry& g) { return g.num_chunks * g.rows_per_chunk * 2; }
 
-// Copies dst[i] <- src[i] of `bytes` each, for i < n, merged into one
-// cudaMemcpyAsync per run of blocks that are adjacent on both sides (slots of
-// a slab are consecutive, and so is the staging), so a group of blocks drains
-// with a handful of DMA operations instead of one per block.
-int copy_runs(void* const* dst, void* const* src, int64_t n, int64_t bytes, cudaStream_t s,
-              const char* what) {
-  for (int64_t i = 0; i < n;) {
-    int64_t j = i + 1;
-    while (j < n && static_cast<uint8_t*>(dst[j]) == static_cast<uint8_t*>(dst[j - 1]) + bytes &&
-           static_cast<uint8_t*>(src[j]) == static_cast<uint8_t*>(src[j - 1]) + bytes)
-      ++j;
-    KVOFF_TRY(cuda_status(cudaMemcpyAsync(dst[i], src[i], (j - i) * bytes, cudaMemcpyDefault, s),
-                          what));
-    i = j;
-  }
-  return KVOFF_OK;
-}
-
-// Two-stage pipeline of the staged calls. The staging buffer is split into two
-// halves. The FP8 kernels run on an auxiliary stream owned by the library (one
-// per caller stream), and events hand each half back and forth between that
-// stream and the caller's stream, so that the kernel of one group overlaps the
-// DMA of the previous group. The ring position persists across calls on the
-// same caller stream and staging buffer, so back-to-back one-block calls
-// alternate halves and overlap too. Everything a call enqueues finishes on the
-// caller's stream, as with the serial path.
-struct Pipe {
-  cudaStream_t aux = nullptr;
-  cudaEvent_t start = nullptr, done = nullptr;
-  cudaEvent_t ready[2] = {nullptr, nullptr};
-  cudaEvent_t freed[2] = {nullptr, nullptr};
-  bool freed_recorded[2] = {false, false};
-  int next = 0;
-  const void* staging = nullptr;
-};
-
-std::mutex g_pipe_mu;
-std::map<std::pair<int, cudaStream_t>, Pipe> g_pipes;
-
-int pipe_for(cudaStream_t caller, const void* staging, Pipe** out) {
-  int dev = 0;
-  KVOFF_TRY(cuda_status(cudaGetDevice(&dev), "cudaGetDevice"));
-  Pipe& p = g_pipes[{dev, caller}];
-  if (p.aux == nullptr) {
-    KVOFF_TRY(cuda_status(cudaStreamCreateWithFlags(&p.aux, cudaStreamNonBlocking),
-                          "cudaStreamCreateWithFlags (pipeline stream)"));
-    cudaEvent_t* events[] = {&p.start, &p.done, &p.ready[0], &p.ready[1], &p.freed[0],
-                             &p.freed[1]};
-    for (cudaEvent_t* e : events)
-      KVOFF_TRY(cuda_status(cudaEventCreateWithFlags(e, cudaEventDisableTiming),
-                            "cudaEventCreateWithFlags (pipeline event)"));
-  }
-  if (p.staging != staging) {  // a new staging buffer starts a fresh ring
-    p.staging = staging;
-    p.freed_recorded[0] = p.freed_recorded[1] = false;
-    p.next = 0;
-  }
-  *out = &p;
-  return KVOFF_OK;
-}
-
 }  // namespace
 }  // namespace kvoff
 
@@ -537,7 +475,7 @@ int kvoff_fp8_save_blocks_staged_ev(const void* pool, int64_t num_chunks, int64_
   const int64_t half = staging_blocks / 2;
   const int64_t cap = pipelined ? half : staging_blocks;
   const int64_t group = cap < kMaxBatch ? cap : kMaxBatch;
-  std::unique_lock<std::mutex> lock(g_pipe_mu, std::defer_lock);
+  std::unique_lock<std::mutex> lock(pipe_mutex(), std::defer_lock);
   Pipe* p = nullptr;
   cudaStream_t ks = s;  // stream that runs the quantize kernels
   if (pipelined) {
@@ -562,8 +500,8 @@ int kvoff_fp8_save_blocks_staged_ev(const void* pool, int64_t num_chunks, int64_
       pdst[i] = static_cast<uint8_t*>(staging_payload) + (h * half + i) * pb;
       sdst[i] = static_cast<uint8_t*>(staging_scale) + (h * half + i) * sb;
     }
-    if (pipelined && p->freed_recorded[h])  // earlier copies out of this half are done
-      KVOFF_TRY(cuda_status(cudaStreamWaitEvent(ks, p->freed[h], 0), "cudaStreamWaitEvent"));
+    if (pipelined)  // earlier copies out of this half are done (and, yielding, the other's)
+      KVOFF_TRY(pipe_wait_half(p, h, ks));
     Args sub = a;
     sub.block_ids = block_ids + first;
     sub.count = n;
@@ -611,7 +549,7 @@ int kvoff_fp8_restore_blocks_staged_ev(void* pool, int64_t num_chunks, int64_t c
   const int64_t half = staging_blocks / 2;
   const int64_t cap = pipelined ? half : staging_blocks;
   const int64_t group = cap < kMaxBatch ? cap : kMaxBatch;
-  std::unique_lock<std::mutex> lock(g_pipe_mu, std::defer_lock);
+  std::unique_lock<std::mutex> lock(pipe_mutex(), std::defer_lock);
   Pipe* p = nullptr;
   cudaStream_t ks = s;  // stream that runs the dequantize kernels
   if (pipelined) {
@@ -627,8 +565,8 @@ int kvoff_fp8_restore_blocks_staged_ev(void* pool, int64_t num_chunks, int64_t c
   for (int64_t first = 0; first < count; first += group) {
     const int64_t n = (count - first) < group ? (count - first) : group;
     const int h = pipelined ? p->next : 0;
-    if (pipelined && p->freed_recorded[h])  // earlier kernels reading this half are done
-      KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p->freed[h], 0), "cudaStreamWaitEvent"));
+    if (pipelined)  // earlier kernels reading this half are done (and, yielding, the other's)
+      KVOFF_TRY(pipe_wait_half(p, h, s));
     for (int64_t i = 0; i < n; ++i) {
       psrc[i] = static_cast<uint8_t*>(staging_payload) + (h * half + i) * pb;
       ssrc[i] = static_cast<uint8_t*>(staging_scale) + (h * half + i) * sb;
@@ -688,15 +626,14 @@ int kvoff_fp8_restore_blocks_staged(void* pool, int64_t num_chunks, int64_t chun
 }
 
 int kvoff_stream_join_pipeline(void* stream) {
-  int dev = 0;
-  KVOFF_TRY(cuda_status(cudaGetDevice(&dev), "cudaGetDevice"));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  std::lock_guard<std::mutex> lock(g_pipe_mu);
-  auto it = g_pipes.find({dev, s});
-  if (it == g_pipes.end()) return ok();
-  Pipe& p = it->second;
-  KVOFF_TRY(cuda_status(cudaEventRecord(p.done, p.aux), "cudaEventRecord"));
-  KVOFF_TRY(cuda_status(cudaStreamWaitEvent(s, p.done, 0), "cudaStreamWaitEvent"));
+  KVOFF_TRY(join_pipe(static_cast<cudaStream_t>(stream)));
+  return ok();
+}
+
+int kvoff_stream_set_yield(void* stream, int32_t enable) {
+  if (enable != 0 && enable != 1)
+    return fail(KVOFF_EINVAL, "kvoff_stream_set_yield: enable must be 0 or 1");
+  KVOFF_TRY(pipe_set_yield(static_cast<cudaStream_t>(stream), enable != 0));
   return ok();
 }
 

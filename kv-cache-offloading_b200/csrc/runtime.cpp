@@ -108,6 +108,87 @@ int64_t streaming_grid(int64_t units, int64_t per_cta, int32_t max_ctas) {
   return grid < 1 ? 1 : grid;
 }
 
+int copy_runs(void* const* dst, void* const* src, int64_t n, int64_t bytes, cudaStream_t s,
+              const char* what) {
+  for (int64_t i = 0; i < n;) {
+    int64_t j = i + 1;
+    while (j < n && static_cast<uint8_t*>(dst[j]) == static_cast<uint8_t*>(dst[j - 1]) + bytes &&
+           static_cast<uint8_t*>(src[j]) == static_cast<uint8_t*>(src[j - 1]) + bytes)
+      ++j;
+    KVOFF_TRY(cuda_status(cudaMemcpyAsync(dst[i], src[i], (j - i) * bytes, cudaMemcpyDefault, s),
+                          what));
+    i = j;
+  }
+  return KVOFF_OK;
+}
+
+namespace {
+std::mutex g_pipe_mu;
+std::map<std::pair<int, cudaStream_t>, Pipe> g_pipes;  // (device, caller stream) -> pipeline
+}  // namespace
+
+std::mutex& pipe_mutex() { return g_pipe_mu; }
+
+namespace {
+int pipe_get(cudaStream_t caller, Pipe** out) {
+  int dev = 0;
+  KVOFF_TRY(cuda_status(cudaGetDevice(&dev), "cudaGetDevice"));
+  Pipe& p = g_pipes[{dev, caller}];
+  if (p.aux == nullptr) {
+    KVOFF_TRY(cuda_status(cudaStreamCreateWithFlags(&p.aux, cudaStreamNonBlocking),
+                          "cudaStreamCreateWithFlags (pipeline stream)"));
+    cudaEvent_t* events[] = {&p.start, &p.done, &p.ready[0], &p.ready[1], &p.freed[0],
+                             &p.freed[1]};
+    for (cudaEvent_t* e : events)
+      KVOFF_TRY(cuda_status(cudaEventCreateWithFlags(e, cudaEventDisableTiming),
+                            "cudaEventCreateWithFlags (pipeline event)"));
+  }
+  *out = &p;
+  return KVOFF_OK;
+}
+}  // namespace
+
+int pipe_for(cudaStream_t caller, const void* staging, Pipe** out) {
+  Pipe* p = nullptr;
+  KVOFF_TRY(pipe_get(caller, &p));
+  if (p->staging != staging) {  // a new staging buffer starts a fresh ring
+    p->staging = staging;
+    p->freed_recorded[0] = p->freed_recorded[1] = false;
+    p->next = 0;
+  }
+  *out = p;
+  return KVOFF_OK;
+}
+
+int pipe_set_yield(cudaStream_t caller, bool yield) {
+  std::lock_guard<std::mutex> lock(g_pipe_mu);
+  Pipe* p = nullptr;
+  KVOFF_TRY(pipe_get(caller, &p));
+  p->yield = yield;
+  return KVOFF_OK;
+}
+
+int pipe_wait_half(Pipe* p, int h, cudaStream_t waiter) {
+  if (p->freed_recorded[h])
+    KVOFF_TRY(cuda_status(cudaStreamWaitEvent(waiter, p->freed[h], 0), "cudaStreamWaitEvent"));
+  if (p->yield && p->freed_recorded[1 - h])
+    KVOFF_TRY(
+        cuda_status(cudaStreamWaitEvent(waiter, p->freed[1 - h], 0), "cudaStreamWaitEvent"));
+  return KVOFF_OK;
+}
+
+int join_pipe(cudaStream_t caller) {
+  int dev = 0;
+  KVOFF_TRY(cuda_status(cudaGetDevice(&dev), "cudaGetDevice"));
+  std::lock_guard<std::mutex> lock(g_pipe_mu);
+  auto it = g_pipes.find({dev, caller});
+  if (it == g_pipes.end()) return KVOFF_OK;
+  Pipe& p = it->second;
+  KVOFF_TRY(cuda_status(cudaEventRecord(p.done, p.aux), "cudaEventRecord"));
+  KVOFF_TRY(cuda_status(cudaStreamWaitEvent(caller, p.done, 0), "cudaStreamWaitEvent"));
+  return KVOFF_OK;
+}
+
 }  // namespace kvoff
 
 using namespace kvoff;

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "kvoff.h"
 
 namespace kvoff {
@@ -38,6 +40,53 @@ int64_t grid_for(int64_t units, const void* kernel, int threads, size_t smem, in
 // limit. On B200 such an oversubscribed grid of short-lived CTAs keeps HBM
 // busier than a persistent grid of resident CTAs.
 int64_t streaming_grid(int64_t units, int64_t per_cta, int32_t max_ctas);
+
+// Copies dst[i] <- src[i] of `bytes` each, for i < n, merged into one
+// cudaMemcpyAsync per run of entries that are adjacent on both sides (slots of
+// a slab are consecutive, and so is a staging buffer), so a group of blocks
+// moves with a handful of DMA operations instead of one per block.
+int copy_runs(void* const* dst, void* const* src, int64_t n, int64_t bytes, cudaStream_t s,
+              const char* what);
+
+// Two-stage pipeline of the staged calls (FP8 and BF16). The caller's staging
+// buffer is split into two halves. Kernels run on an auxiliary stream owned by
+// the library (one per device and caller stream), and events hand each half
+// back and forth between that stream and the caller's stream, so that the
+// kernel of one group overlaps the DMA of the previous group. The ring
+// position persists across calls on the same caller stream and staging buffer,
+// so back-to-back one-block calls alternate halves and overlap too.
+struct Pipe {
+  cudaStream_t aux = nullptr;
+  cudaEvent_t start = nullptr, done = nullptr;
+  cudaEvent_t ready[2] = {nullptr, nullptr};
+  cudaEvent_t freed[2] = {nullptr, nullptr};
+  bool freed_recorded[2] = {false, false};
+  int next = 0;
+  const void* staging = nullptr;
+  // Yield: each group's DMA waits for the previous group's kernel (restore)
+  // or each group's kernel for the previous group's DMA (save), so the copy
+  // engine goes idle between groups (see kvoff_stream_set_yield).
+  bool yield = false;
+};
+
+// Guards every Pipe; hold it from pipe_for until the call has enqueued its work.
+std::mutex& pipe_mutex();
+
+// The pipeline of (current device, caller); a new staging buffer starts a
+// fresh ring. Creates the stream and events on first use.
+int pipe_for(cudaStream_t caller, const void* staging, Pipe** out);
+
+// Makes `caller` wait for everything its pipeline queued on the auxiliary
+// stream (no-op without one). Takes pipe_mutex() itself.
+int join_pipe(cudaStream_t caller);
+
+// Sets the yield flag of (current device, caller)'s pipeline, creating it if
+// needed without touching its ring. Takes pipe_mutex() itself.
+int pipe_set_yield(cudaStream_t caller, bool yield);
+
+// Before a group reuses staging half h, makes `waiter` wait for the last work
+// that used half h and, with yield on, for the last work on the other half.
+int pipe_wait_half(Pipe* p, int h, cudaStream_t waiter);
 
 }  // namespace kvoff
 

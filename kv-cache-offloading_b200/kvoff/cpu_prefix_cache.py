@@ -85,17 +85,21 @@ class _FollowerManager:
 
 # Copy methods for CUDA pools. FP8: "staged" (kernel into device staging,
 # DMA drain) or "mapped" (kernel reads/writes the pinned slot over PCIe).
-# BF16: "engine" (one strided DMA per block), "tma" (cp.async.bulk gather into
-# device staging + DMA) or "sm" (vector-copy kernel over PCIe). Override with
+# BF16: "staged" (TMA gather / scatter kernels on one half of a device staging
+# buffer while plain DMA moves the other half, one native call), "engine" (one
+# strided DMA per block), "tma" (the TMA kernel and the DMA as separate calls
+# in stream order) or "sm" (vector-copy kernel over PCIe). Override with
 # KVOFF_FP8_SAVE / KVOFF_FP8_RESTORE / KVOFF_BF16_SAVE / KVOFF_BF16_RESTORE.
-# BF16 restores default to "tma": a strided (2D) DMA into the pool holds up the
-# compute stream's own small host-to-device copies queued behind it, so a
-# prefill that overlaps a run of restores stalls until they drain; a plain
-# DMA into staging plus the scatter kernel lets it run alongside.
+# BF16 defaults to "staged": a strided (2D) DMA straight into or out of the
+# pool holds up the compute stream's own small copies queued behind it, so a
+# prefill that overlaps a run of restores stalls until they drain; and a
+# staged save frees its block for reuse once the gather kernel has read it,
+# not after the drain to host.
 DEFAULT_MODES = {"fp8_save": "staged", "fp8_restore": "staged",
-                 "bf16_save": "engine", "bf16_restore": "tma"}
+                 "bf16_save": "staged", "bf16_restore": "staged"}
 _MODE_CHOICES = {"fp8_save": ("staged", "mapped"), "fp8_restore": ("staged", "mapped"),
-                 "bf16_save": ("engine", "tma", "sm"), "bf16_restore": ("engine", "tma", "sm")}
+                 "bf16_save": ("staged", "engine", "tma", "sm"),
+                 "bf16_restore": ("staged", "engine", "tma", "sm")}
 
 
 def _transfer_modes() -> dict[str, str]:
@@ -212,6 +216,15 @@ class CPUBlockCache:
             self._restore_stream = (torch.cuda.Stream(pool.device) if split_streams
                                     else self._copy_stream)
             self._ready = torch.cuda.Event()  # re-recorded before each staged save
+            # Yield mode (kvoff_stream_set_yield) leaves the copy engine idle
+            # between blocks, so the engine's per-step input and sampled-token
+            # copies are not held behind a run of block transfers. It pays for
+            # BF16 blocks, whose transfers are twice as long; for FP8 blocks
+            # the gaps cost more than the stalls they remove. KVOFF_COPY_YIELD
+            # (0 or 1) overrides the choice.
+            if os.environ.get("KVOFF_COPY_YIELD", "0" if fp8 else "1") != "0":
+                for stream in {self._copy_stream, self._restore_stream}:
+                    ops.set_yield(pool.device, stream, True)
 
     # -- tensor parallelism ----------------------------------------------------
     #
@@ -419,7 +432,7 @@ class CPUBlockCache:
                      source_done=None):
         """Enqueue pool blocks -> slots on `stream` (one native call per method).
 
-        wait_events / source_done apply to staged FP8 saves (ops.save_fp8_staged).
+        wait_events / source_done apply to staged saves (FP8 and BF16).
         """
         ops, modes = self._ops, self._modes
         if self._fp8:
@@ -433,7 +446,10 @@ class CPUBlockCache:
             return
         method = modes["bf16_save"]
         payload, _ = self._pointers(slots, method == "sm")
-        if method == "tma":
+        if method == "staged":
+            self._staged_call(True, pool, block_ids, payload, None, stream, wait_events or (),
+                              source_done)
+        elif method == "tma":
             staged, _ = self._stage(stream, len(block_ids))
             for first in range(0, len(block_ids), len(staged)):
                 ids = block_ids[first:first + len(staged)]
@@ -450,7 +466,7 @@ class CPUBlockCache:
                         done_event=None):
         """Enqueue slots -> pool blocks on `stream`; plain / mapped are the slots'
         (payload, scale) host pointers and device aliases. done_event applies to
-        staged FP8 restores (ops.restore_fp8_staged)."""
+        staged restores (FP8 and BF16)."""
         ops, modes = self._ops, self._modes
         if self._fp8:
             if modes["fp8_restore"] == "mapped":
@@ -459,7 +475,9 @@ class CPUBlockCache:
                 self._staged_call(False, pool, block_ids, *plain, stream, (), done_event)
             return
         method = modes["bf16_restore"]
-        if method == "tma":
+        if method == "staged":
+            self._staged_call(False, pool, block_ids, plain[0], None, stream, (), done_event)
+        elif method == "tma":
             staged, _ = self._stage(stream, len(block_ids))
             for first in range(0, len(block_ids), len(staged)):
                 ids = block_ids[first:first + len(staged)]
@@ -476,33 +494,39 @@ class CPUBlockCache:
 
     def _staged_call(self, save: bool, pool: torch.Tensor, block_ids, payload, scale, stream,
                      wait_events, event):
-        """One staged FP8 call through ops._fp8_staged_ev (raw handles, the
-        cache's own geometry, no per-call tensor checks). wait_events and
-        event are recorded torch.cuda.Events or None."""
+        """One staged call (FP8: ops._fp8_staged_ev; BF16: ops._copy_staged_ev,
+        with scale None) with raw handles, the cache's own geometry and no
+        per-call tensor checks. wait_events and event are recorded
+        torch.cuda.Events or None."""
         staged_payload, staged_scale = self._stage(stream, len(block_ids))
         g = self._geometry if pool is self._cache else self._ops.geometry(pool)
         waits = [e.cuda_event for e in wait_events]
+        handle = event.cuda_event if event is not None else 0
         index = pool.device.index
         guard = (contextlib.nullcontext() if torch.cuda.current_device() == index
                  else torch.cuda.device(index))
         with guard:
-            self._ops._fp8_staged_ev(save, g, pool.data_ptr(), block_ids, payload, scale,
-                                     staged_payload.data_ptr(), staged_scale.data_ptr(),
-                                     min(staged_payload.shape[0], staged_scale.shape[0]),
-                                     stream.cuda_stream, waits,
-                                     event.cuda_event if event is not None else 0)
+            if scale is None:
+                self._ops._copy_staged_ev(save, g, pool.data_ptr(), block_ids, payload,
+                                          staged_payload.data_ptr(), staged_payload.shape[0],
+                                          stream.cuda_stream, waits, handle)
+            else:
+                self._ops._fp8_staged_ev(save, g, pool.data_ptr(), block_ids, payload, scale,
+                                         staged_payload.data_ptr(), staged_scale.data_ptr(),
+                                         min(staged_payload.shape[0], staged_scale.shape[0]),
+                                         stream.cuda_stream, waits, handle)
 
     def _restore_slots(self, slots, block_ids, stream) -> torch.cuda.Event:
         """Restore slots into pool blocks on `stream`; returns the done event.
 
-        A staged FP8 restore records the event after its last dequantize kernel
-        (on the library's kernel stream), so `stream` is free to start the next
-        restore's copies while those kernels run; other methods record it on
-        `stream` after the copies.
+        A staged restore (FP8 or BF16) records the event after its last
+        dequantize or scatter kernel (on the library's kernel stream), so
+        `stream` is free to start the next restore's copies while those kernels
+        run; other methods record it on `stream` after the copies.
         """
         done = torch.cuda.Event()
         done.record(stream)  # creates the CUDA event; a staged restore re-records it
-        staged = self._fp8 and self._modes["fp8_restore"] == "staged"
+        staged = self._modes["fp8_restore" if self._fp8 else "bf16_restore"] == "staged"
         self._device_restore(self._cache, block_ids, self._pointers(slots, False),
                              self._pointers(slots, True), stream,
                              done_event=done if staged else None)
@@ -686,14 +710,14 @@ class CPUBlockCache:
         The copies follow the kernels that wrote the blocks and, with split
         streams, earlier restores that read these slots. before_block_reuse
         orders each block's next writer after the point where the save has read
-        it: for staged FP8 that is the quantize kernel (the library records
-        `read` after it, while the copies to host still drain); otherwise the
-        returned event.
+        it: for a staged save that is the quantize or gather kernel (the
+        library records `read` after it, while the copies to host still
+        drain); otherwise the returned event.
         """
         pool = self._cache
         current = torch.cuda.current_stream(pool.device)
         copy = self._copy_stream
-        staged = self._fp8 and self._modes["fp8_save"] == "staged"
+        staged = self._modes["fp8_save" if self._fp8 else "bf16_save"] == "staged"
         waits = read = None
         if staged:
             # The kernels wait only for the blocks' writers (and restores still

@@ -239,6 +239,13 @@ def join_pipeline(device, stream=None) -> None:
         _lib.call("kvoff_stream_join_pipeline", _stream(device, stream))
 
 
+def set_yield(device, stream, enable: bool) -> None:
+    """Yield mode of the staged calls on `stream` (kvoff_stream_set_yield)."""
+    device = torch.device(device)
+    with torch.cuda.device(device):
+        _lib.call("kvoff_stream_set_yield", _stream(device, stream), 1 if enable else 0)
+
+
 def copy_blocks(pool: torch.Tensor, block_ids, slot_ptrs, *, restore: bool = False,
                 method: int = COPY_ENGINE, stream=None, max_ctas: int = 0) -> None:
     """Byte-exact block moves pool <-> dense slots (BF16 passthrough)."""
@@ -253,6 +260,52 @@ def copy_blocks(pool: torch.Tensor, block_ids, slot_ptrs, *, restore: bool = Fal
                   g.block_stride * e, g.num_blocks, g.chunk_bytes, _lib.int64_array(block_ids), n,
                   _lib.pointer_array(slot_ptrs), _lib.RESTORE if restore else _lib.SAVE, method,
                   max_ctas, _stream(pool.device, stream))
+
+
+def copy_blocks_staged(pool: torch.Tensor, block_ids, host_slot_ptrs, staging: torch.Tensor, *,
+                       restore: bool = False, stream=None, wait_events=(), event=None) -> None:
+    """Byte-exact block moves pool <-> pinned host slots through device staging.
+
+    staging is a [n, block_bytes] uint8 device buffer; with n >= 2 the gather /
+    scatter kernels of one half overlap the DMA of the other (a library-owned
+    kernel stream; see join_pipeline). Save: the kernels wait for wait_events
+    (recorded torch.cuda.Events; none: earlier work on the stream) and `event`
+    is recorded once the pool blocks are read. Restore: `event` is recorded
+    after the last pool write and the stream is not joined; without it the
+    stream waits for the kernels.
+    """
+    _require_cuda(pool, "pool")
+    _require_cuda(staging, "staging")
+    g = geometry(pool)
+    n = len(block_ids)
+    if len(host_slot_ptrs) != n:
+        raise ValueError("one slot pointer per block")
+    if staging.dtype != torch.uint8 or staging.dim() != 2 or staging.shape[1] != g.block_bytes:
+        raise ValueError(f"staging must be uint8 [n, {g.block_bytes}]")
+    if restore and wait_events:
+        raise ValueError("wait_events apply to saves only")
+    with torch.cuda.device(pool.device):
+        _copy_staged_ev(not restore, g, pool.data_ptr(), block_ids, host_slot_ptrs,
+                        staging.data_ptr(), staging.shape[0], _stream(pool.device, stream),
+                        [_event(e) for e in wait_events], _event(event) if event is not None else 0)
+
+
+def _copy_staged_ev(save: bool, g: PoolGeometry, pool_ptr: int, block_ids, slot_ptrs,
+                    staging_ptr: int, staging_blocks: int, stream: int, wait_events=(),
+                    event: int = 0) -> None:
+    """Lean form of copy_blocks_staged for the drop-in cache's per-block path
+    (checked geometry, raw pointers, stream and event handles, the pool's
+    device current)."""
+    n = len(block_ids)
+    ids = (ctypes.c_int64 * n)(*block_ids)
+    slots = (ctypes.c_void_p * n)(*slot_ptrs)
+    waits = (ctypes.c_void_p * max(1, len(wait_events)))(*wait_events)
+    e = g.elem_size
+    rc = _lib.lib().kvoff_copy_blocks_staged(
+        pool_ptr, g.num_chunks, g.chunk_stride * e, g.block_stride * e, g.num_blocks,
+        g.chunk_bytes, ids, n, slots, staging_ptr, staging_blocks,
+        _lib.SAVE if save else _lib.RESTORE, waits, len(wait_events), event or None, stream)
+    _lib.check(rc, "kvoff_copy_blocks_staged")
 
 
 def copy_tokens(pool: torch.Tensor, block_ids, num_tokens: int, dense_ptr: int, *,

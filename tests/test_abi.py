@@ -116,6 +116,35 @@ def test_event_ordered_entry_points_check_their_arguments_on_the_host():
     assert rc == _lib.KVOFF_EINVAL and "out of range" in _lib.last_error()
 
 
+def test_staged_block_copies_check_their_arguments_on_the_host():
+    so = _lib.lib()
+    ids = _lib.int64_array([0])
+    slots = _lib.pointer_array([16])
+    geom = (ctypes.c_void_p(256), 4, 4096, 1024, 4, 1024)
+    # Bad direction, wait events on a restore, and a null staging buffer are
+    # rejected before any device work; an empty batch is a no-op.
+    rc = so.kvoff_copy_blocks_staged(*geom, ids, 1, slots, ctypes.c_void_p(512), 2, 7, None, 0,
+                                     None, None)
+    assert rc == _lib.KVOFF_EINVAL and "direction" in _lib.last_error()
+    rc = so.kvoff_copy_blocks_staged(*geom, ids, 1, slots, ctypes.c_void_p(512), 2, _lib.RESTORE,
+                                     slots, 1, None, None)
+    assert rc == _lib.KVOFF_EINVAL and "wait event" in _lib.last_error()
+    rc = so.kvoff_copy_blocks_staged(*geom, ids, 1, slots, None, 2, _lib.SAVE, None, 0, None,
+                                     None)
+    assert rc == _lib.KVOFF_EINVAL and "staging" in _lib.last_error()
+    assert so.kvoff_copy_blocks_staged(*geom, ids, 0, slots, None, 2, _lib.SAVE, None, 0, None,
+                                       None) == _lib.KVOFF_OK
+    bad = _lib.int64_array([4])
+    rc = so.kvoff_copy_blocks_staged(*geom, bad, 1, slots, ctypes.c_void_p(512), 2, _lib.SAVE,
+                                     None, 0, None, None)
+    assert rc == _lib.KVOFF_EINVAL and "out of range" in _lib.last_error()
+
+
+def test_yield_mode_rejects_values_other_than_zero_and_one():
+    assert _lib.lib().kvoff_stream_set_yield(None, 2) == _lib.KVOFF_EINVAL
+    assert "0 or 1" in _lib.last_error()
+
+
 def test_ops_rejects_events_that_were_never_recorded():
     from kvoff import ops
 

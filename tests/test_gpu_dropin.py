@@ -58,7 +58,7 @@ def slow_copies(cache, names=("save_block", "_copy_entry")):
 SHAPES = [(2, 2, 4, 256, 1, 4), (2, 3, 6, 256, 8, 128)]
 
 
-@pytest.mark.parametrize("method", ["engine", "tma", "sm"])
+@pytest.mark.parametrize("method", ["staged", "engine", "tma", "sm"])
 @pytest.mark.parametrize("shape", SHAPES)
 def test_bf16_round_trip_byte_exact(cuda, monkeypatch, method, shape):
     monkeypatch.setenv("KVOFF_BF16_SAVE", method)
@@ -217,6 +217,31 @@ def test_fp8_block_reuse_waits_for_the_read_not_the_drain(cuda):
     assert np.array_equal(bits_u16(entry.scale), want_s[0])
 
 
+def test_bf16_staged_block_reuse_waits_for_the_gather_not_the_drain(cuda):
+    """Staged BF16: before_block_reuse waits for the gather kernel alone, as
+    for staged FP8; the slot still receives the block as it was when saved."""
+    engine = FakeEngine(arbitrary_pool(SHAPES[1], cuda))
+    m = engine.manager
+    key = m.publish(3)
+    expected = block_bytes(engine.pool, 3)
+    cache = engine.create_cpu_prefix_cache(per_block(engine.pool), split_streams=True,
+                                           preallocate=True)
+    assert cache._modes["bf16_save"] == "staged"
+    assert cache.save_block(key)  # allocates the staging buffers outside the timed part
+    cache.synchronize()
+    assert cache.discard(key)
+    with torch.cuda.stream(cache._copy_stream):
+        torch.cuda._sleep(5 * SLEEP_CYCLES)
+    assert cache.save_block(key)
+    cache.before_block_reuse(3)
+    engine.pool[:, :, 3].fill_(5)  # the block's next writer
+    torch.cuda.current_stream(cuda).synchronize()
+    assert not cache._copy_stream.query()  # the drain has not finished
+    cache.synchronize()
+    payload, _ = cache._slot_view(cache._entries[key].slot)
+    assert torch.equal(payload.view(torch.uint8).reshape(-1), expected.reshape(-1))
+
+
 @pytest.mark.parametrize("split", [True, False])
 def test_fp8_back_to_back_restores_match_oracle(cuda, split):
     """Per-block staged restores share two staging halves without a join per
@@ -258,19 +283,23 @@ def test_fp8_back_to_back_restores_match_oracle(cuda, split):
     assert np.array_equal(bits_u16(entry.scale), want_s[0])
 
 
-def test_injected_failures_roll_back_and_retry_is_byte_exact(cuda):
+@pytest.mark.parametrize("method", ["staged", "engine"])
+def test_injected_failures_roll_back_and_retry_is_byte_exact(cuda, monkeypatch, method):
+    monkeypatch.setenv("KVOFF_BF16_SAVE", method)
+    monkeypatch.setenv("KVOFF_BF16_RESTORE", method)
+    op = {"staged": "copy_blocks_staged", "engine": "copy_blocks"}[method]
     engine = FakeEngine(arbitrary_pool(SHAPES[1], cuda))
     m = engine.manager
     key = m.publish(1)
     cache = engine.create_cpu_prefix_cache(per_block(engine.pool))
     expected = block_bytes(engine.pool, 1)
-    kvoff.debug_fail_next("copy_blocks", 1)
+    kvoff.debug_fail_next(op, 1)
     with pytest.raises(RuntimeError, match="injected"):
         cache.save_block(key)
     assert len(cache) == cache.bytes_used == 0 and key in m.hash_to_block_id
     assert cache.save_block(key)
     m.forget(key)
-    kvoff.debug_fail_next("copy_blocks", 1)
+    kvoff.debug_fail_next(op, 1)
     with pytest.raises(kvoff.KvoffError, match="injected"):
         cache.restore_block(key)
     assert key in cache and key not in m.hash_to_block_id
@@ -322,7 +351,8 @@ def test_prefetch_restore_orders_first_use(cuda):
     assert torch.equal(got, expected)
 
 
-@pytest.mark.parametrize("modes", [("staged", "engine"), ("mapped", "sm"), ("staged", "tma")])
+@pytest.mark.parametrize("modes", [("staged", "staged"), ("staged", "engine"), ("mapped", "sm"),
+                                   ("staged", "tma")])
 @pytest.mark.parametrize("fp8", [False, True])
 def test_batched_calls_match_per_block_calls(cuda, monkeypatch, modes, fp8):
     fp8_mode, bf16_mode = modes

@@ -201,8 +201,21 @@ def test_fp8_staged_and_mapped_pinned_slots(cuda):
     assert np.array_equal(u16(pool), bits)
 
 
-def test_fp8_staged_pipeline_over_many_groups_and_calls(cuda):
-    """Staging of 4 blocks runs as a two-half pipeline (kernels on a library stream)."""
+@pytest.mark.parametrize("yielding", [False, True])
+def test_fp8_staged_pipeline_over_many_groups_and_calls(cuda, yielding):
+    """Staging of 4 blocks runs as a two-half pipeline (kernels on a library
+    stream), with and without yield mode."""
+    from kvoff import ops
+
+    stream = torch.cuda.Stream(cuda)
+    ops.set_yield(cuda, stream, yielding)
+    try:
+        _fp8_staged_pipeline(cuda, stream)
+    finally:
+        ops.set_yield(cuda, stream, False)
+
+
+def _fp8_staged_pipeline(cuda, stream):
     from kvoff import ops
     from kvoff.slab import PinnedSlab
 
@@ -216,7 +229,6 @@ def test_fp8_staged_pipeline_over_many_groups_and_calls(cuda):
     scale = [slab.view(7 * g.fp8_payload_bytes + i * g.fp8_scale_bytes, (g.fp8_scale_bytes,),
                        torch.uint8) for i in range(7)]
     staging = empty_slots(4, g, cuda)
-    stream = torch.cuda.Stream(cuda)
     ids = [11, 3, 7, 0, 5, 9, 1]
     want_p, want_s = oracle.fp8_save_blocks(bits, ids)
     for chunk in ([0, 1, 2, 3, 4], [5], [6]):  # one multi-group call, then two one-block calls
@@ -329,6 +341,56 @@ def test_bf16_passthrough_byte_exact(cuda, method, shape):
     assert np.array_equal(u16(pool), bits)
     from kvoff import device_error
     assert device_error(0) == 0
+
+
+@pytest.mark.parametrize("staging_blocks", [1, 2, 3, 8])
+@pytest.mark.parametrize("misaligned", [False, True])
+@pytest.mark.parametrize("yielding", [False, True])
+def test_bf16_staged_copies_byte_exact(cuda, staging_blocks, misaligned, yielding):
+    """kvoff_copy_blocks_staged: one and two-half staging, groups smaller than
+    the batch, back-to-back calls on one ring, a pool whose base is only
+    2-byte aligned (the SM-kernel fallback instead of TMA), with and without
+    yield mode."""
+    from kvoff import device_error, ops
+
+    ops.set_yield(cuda, None, yielding)
+    try:
+        _bf16_staged_round_trip(cuda, staging_blocks, misaligned)
+    finally:
+        ops.set_yield(cuda, None, False)
+    assert device_error(0) == 0
+
+
+def _bf16_staged_round_trip(cuda, staging_blocks, misaligned):
+    from kvoff import ops
+    from kvoff.slab import PinnedSlab
+
+    shape = (2, 3, 9, 256, 2, 64)
+    rng = np.random.default_rng(staging_blocks)
+    bits = rng.integers(0, 1 << 16, shape).astype(np.uint16)
+    if misaligned:  # same pool, one element into a larger buffer
+        flat = torch.empty(int(np.prod(shape)) + 1, dtype=torch.bfloat16, device=cuda)
+        pool = flat[1:].view(shape)
+        pool.copy_(to_bf16(bits, cuda))
+    else:
+        pool = to_bf16(bits, cuda)
+    g = ops.geometry(pool)
+    ids, targets = [8, 0, 3, 5, 1], [2, 4, 6, 7, 0]
+    slab = PinnedSlab(len(ids) * g.block_bytes, device=0)
+    host = slab.view(0, (len(ids), g.block_bytes), torch.uint8)
+    host.fill_(0xA5)
+    staging = torch.empty((staging_blocks, g.block_bytes), dtype=torch.uint8, device=cuda)
+    ptrs = [h.data_ptr() for h in host]
+    ops.copy_blocks_staged(pool, ids[:2], ptrs[:2], staging)  # two calls share the ring
+    ops.copy_blocks_staged(pool, ids[2:], ptrs[2:], staging)
+    torch.cuda.synchronize()
+    want = oracle.copy_blocks(bits, ids)
+    assert np.array_equal(host.numpy().view(np.uint16).reshape(want.shape), want)
+    ops.copy_blocks_staged(pool, targets, ptrs, staging, restore=True)
+    oracle.copy_blocks(bits, targets, want, restore=True)
+    ops.join_pipeline(cuda)
+    torch.cuda.synchronize()
+    assert np.array_equal(u16(pool), bits)
 
 
 def test_bounded_device_wait_reports_a_timeout_and_the_context_survives(cuda):
