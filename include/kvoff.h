@@ -217,22 +217,19 @@ KVOFF_API int kvoff_fp8_restore_blocks_staged_ev(void* pool, int64_t num_chunks,
  * Make `stream` wait for all work the staged calls queued on their internal
  * kernel stream for `stream` (needed before synchronizing `stream` or freeing
  * its staging buffers after *_ev calls). No-op when there is none.
+ *
+ * The staged calls (FP8 and BF16) pipeline their kernels on that internal
+ * stream when staging_blocks >= 2. With staging_blocks = 1 they run serially
+ * on `stream` itself, one block at a time: the copy engine then goes idle
+ * while each block's kernel runs, so small copies that other streams queue on
+ * it meanwhile (a compute stream's per-step inputs and sampled tokens) run in
+ * those gaps instead of waiting behind a whole run of block transfers, as
+ * with the reference, whose copies and kernels share one stream
+ * (cpu_prefix_cache.py:236-243, :311-322). Join before switching a stream
+ * and staging buffer between the two forms.
  */
 KVOFF_API int kvoff_stream_join_pipeline(void* stream);
 
-/*
- * Yield mode for the staged calls on `stream` (FP8 and BF16; off by default).
- * With it on, each group's host copy on `stream` starts only after the
- * previous group's kernel has finished (restore), and each group's kernel
- * only after the previous group's host copy (save). The copy engine then goes
- * idle for one kernel's duration between groups, so small copies that other
- * streams queue on it meanwhile (a compute stream's per-step inputs and
- * sampled tokens) run there instead of waiting behind a whole run of block
- * transfers. It costs a few percent of a long run's throughput. The
- * reference's restores and saves leave the same gaps, because their copies
- * and kernels share one stream (cpu_prefix_cache.py:236-243, :311-322).
- */
-KVOFF_API int kvoff_stream_set_yield(void* stream, int32_t enable);
 
 /*
  * Byte-exact block passthrough (BF16 mode): move whole blocks between the

@@ -396,16 +396,15 @@ int kvoff_copy_blocks_staged(void* pool, int64_t num_chunks, int64_t chunk_strid
   uint8_t* stage = static_cast<uint8_t*>(staging);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool save = direction == KVOFF_SAVE;
-  const bool pipelined = staging_blocks >= 2;
+  std::unique_lock<std::mutex> lock(pipe_mutex(), std::defer_lock);
+  Pipe* p = nullptr;
+  KVOFF_TRY(pipe_begin(s, staging, staging_blocks, lock, &p));
+  const bool pipelined = p != nullptr;
   const int64_t half = staging_blocks / 2;
   const int64_t cap = pipelined ? half : staging_blocks;
   const int64_t group = cap < kMaxBatch ? cap : kMaxBatch;
-  std::unique_lock<std::mutex> lock(pipe_mutex(), std::defer_lock);
-  Pipe* p = nullptr;
   cudaStream_t ks = s;  // stream that runs the gather / scatter kernels
   if (pipelined) {
-    lock.lock();
-    KVOFF_TRY(pipe_for(s, staging, &p));
     ks = p->aux;
   }
   if (num_wait_events > 0) {  // a save's kernels need only these, not earlier DMA on `s`
@@ -422,7 +421,7 @@ int kvoff_copy_blocks_staged(void* pool, int64_t num_chunks, int64_t chunk_strid
     const int h = pipelined ? p->next : 0;
     for (int64_t i = 0; i < n; ++i) dense[i] = stage + (h * half + i) * bb;
     if (save) {
-      if (pipelined)  // earlier copies out of this half are done (and, yielding, the other's)
+      if (pipelined)  // earlier copies out of this half are done
         KVOFF_TRY(pipe_wait_half(p, h, ks));
       KVOFF_TRY(copy_kernel(base, g, block_ids + first, n, dense, true, method, 0, ks));
       if (event != nullptr && first + n >= count)  // every pool block has been read
@@ -439,7 +438,7 @@ int kvoff_copy_blocks_staged(void* pool, int64_t num_chunks, int64_t chunk_strid
         p->next = 1 - h;
       }
     } else {
-      if (pipelined)  // earlier kernels reading this half are done (and, yielding, the other's)
+      if (pipelined)  // earlier kernels reading this half are done
         KVOFF_TRY(pipe_wait_half(p, h, s));
       KVOFF_TRY(copy_runs(dense, host_slots + first, n, bb, s, "staged block restore copy"));
       if (pipelined) {

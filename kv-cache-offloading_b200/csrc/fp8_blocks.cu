@@ -471,16 +471,15 @@ int kvoff_fp8_save_blocks_staged_ev(const void* pool, int64_t num_chunks, int64_
                   (long long)i);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t pb = payload_bytes(a.g), sb = scale_bytes(a.g);
-  const bool pipelined = staging_blocks >= 2;
+  std::unique_lock<std::mutex> lock(pipe_mutex(), std::defer_lock);
+  Pipe* p = nullptr;
+  KVOFF_TRY(pipe_begin(s, staging_payload, staging_blocks, lock, &p));
+  const bool pipelined = p != nullptr;
   const int64_t half = staging_blocks / 2;
   const int64_t cap = pipelined ? half : staging_blocks;
   const int64_t group = cap < kMaxBatch ? cap : kMaxBatch;
-  std::unique_lock<std::mutex> lock(pipe_mutex(), std::defer_lock);
-  Pipe* p = nullptr;
   cudaStream_t ks = s;  // stream that runs the quantize kernels
   if (pipelined) {
-    lock.lock();
-    KVOFF_TRY(pipe_for(s, staging_payload, &p));
     ks = p->aux;
   }
   if (num_wait_events > 0) {  // the kernels need only these, not earlier DMA on `s`
@@ -500,7 +499,7 @@ int kvoff_fp8_save_blocks_staged_ev(const void* pool, int64_t num_chunks, int64_
       pdst[i] = static_cast<uint8_t*>(staging_payload) + (h * half + i) * pb;
       sdst[i] = static_cast<uint8_t*>(staging_scale) + (h * half + i) * sb;
     }
-    if (pipelined)  // earlier copies out of this half are done (and, yielding, the other's)
+    if (pipelined)  // earlier copies out of this half are done
       KVOFF_TRY(pipe_wait_half(p, h, ks));
     Args sub = a;
     sub.block_ids = block_ids + first;
@@ -545,16 +544,15 @@ int kvoff_fp8_restore_blocks_staged_ev(void* pool, int64_t num_chunks, int64_t c
                   (long long)i);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t pb = payload_bytes(a.g), sb = scale_bytes(a.g);
-  const bool pipelined = staging_blocks >= 2;
+  std::unique_lock<std::mutex> lock(pipe_mutex(), std::defer_lock);
+  Pipe* p = nullptr;
+  KVOFF_TRY(pipe_begin(s, staging_payload, staging_blocks, lock, &p));
+  const bool pipelined = p != nullptr;
   const int64_t half = staging_blocks / 2;
   const int64_t cap = pipelined ? half : staging_blocks;
   const int64_t group = cap < kMaxBatch ? cap : kMaxBatch;
-  std::unique_lock<std::mutex> lock(pipe_mutex(), std::defer_lock);
-  Pipe* p = nullptr;
   cudaStream_t ks = s;  // stream that runs the dequantize kernels
   if (pipelined) {
-    lock.lock();
-    KVOFF_TRY(pipe_for(s, staging_payload, &p));
     ks = p->aux;
     // Kernels write the pool: order them after the caller stream's earlier work.
     KVOFF_TRY(cuda_status(cudaEventRecord(p->start, s), "cudaEventRecord"));
@@ -565,7 +563,7 @@ int kvoff_fp8_restore_blocks_staged_ev(void* pool, int64_t num_chunks, int64_t c
   for (int64_t first = 0; first < count; first += group) {
     const int64_t n = (count - first) < group ? (count - first) : group;
     const int h = pipelined ? p->next : 0;
-    if (pipelined)  // earlier kernels reading this half are done (and, yielding, the other's)
+    if (pipelined)  // earlier kernels reading this half are done
       KVOFF_TRY(pipe_wait_half(p, h, s));
     for (int64_t i = 0; i < n; ++i) {
       psrc[i] = static_cast<uint8_t*>(staging_payload) + (h * half + i) * pb;
@@ -630,12 +628,6 @@ int kvoff_stream_join_pipeline(void* stream) {
   return ok();
 }
 
-int kvoff_stream_set_yield(void* stream, int32_t enable) {
-  if (enable != 0 && enable != 1)
-    return fail(KVOFF_EINVAL, "kvoff_stream_set_yield: enable must be 0 or 1");
-  KVOFF_TRY(pipe_set_yield(static_cast<cudaStream_t>(stream), enable != 0));
-  return ok();
-}
 
 }  // extern "C"
 

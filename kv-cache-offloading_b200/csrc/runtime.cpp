@@ -160,20 +160,18 @@ int pipe_for(cudaStream_t caller, const void* staging, Pipe** out) {
   return KVOFF_OK;
 }
 
-int pipe_set_yield(cudaStream_t caller, bool yield) {
-  std::lock_guard<std::mutex> lock(g_pipe_mu);
-  Pipe* p = nullptr;
-  KVOFF_TRY(pipe_get(caller, &p));
-  p->yield = yield;
-  return KVOFF_OK;
-}
-
 int pipe_wait_half(Pipe* p, int h, cudaStream_t waiter) {
   if (p->freed_recorded[h])
     KVOFF_TRY(cuda_status(cudaStreamWaitEvent(waiter, p->freed[h], 0), "cudaStreamWaitEvent"));
-  if (p->yield && p->freed_recorded[1 - h])
-    KVOFF_TRY(
-        cuda_status(cudaStreamWaitEvent(waiter, p->freed[1 - h], 0), "cudaStreamWaitEvent"));
+  return KVOFF_OK;
+}
+
+int pipe_begin(cudaStream_t caller, const void* staging, int64_t staging_blocks,
+               std::unique_lock<std::mutex>& lock, Pipe** out) {
+  *out = nullptr;
+  if (staging_blocks < 2) return KVOFF_OK;
+  lock.lock();
+  KVOFF_TRY(pipe_for(caller, staging, out));
   return KVOFF_OK;
 }
 

@@ -63,10 +63,6 @@ struct Pipe {
   bool freed_recorded[2] = {false, false};
   int next = 0;
   const void* staging = nullptr;
-  // Yield: each group's DMA waits for the previous group's kernel (restore)
-  // or each group's kernel for the previous group's DMA (save), so the copy
-  // engine goes idle between groups (see kvoff_stream_set_yield).
-  bool yield = false;
 };
 
 // Guards every Pipe; hold it from pipe_for until the call has enqueued its work.
@@ -80,13 +76,15 @@ int pipe_for(cudaStream_t caller, const void* staging, Pipe** out);
 // stream (no-op without one). Takes pipe_mutex() itself.
 int join_pipe(cudaStream_t caller);
 
-// Sets the yield flag of (current device, caller)'s pipeline, creating it if
-// needed without touching its ring. Takes pipe_mutex() itself.
-int pipe_set_yield(cudaStream_t caller, bool yield);
-
 // Before a group reuses staging half h, makes `waiter` wait for the last work
-// that used half h and, with yield on, for the last work on the other half.
+// that used half h.
 int pipe_wait_half(Pipe* p, int h, cudaStream_t waiter);
+
+// Starts a staged call on `caller`. Returns in *out the pipeline, with `lock`
+// (on pipe_mutex()) held, or nullptr when the call runs serially on `caller`
+// (a one-block staging buffer).
+int pipe_begin(cudaStream_t caller, const void* staging, int64_t staging_blocks,
+               std::unique_lock<std::mutex>& lock, Pipe** out);
 
 }  // namespace kvoff
 

@@ -47,7 +47,6 @@ SIGNATURES = {
                                                           _PI64, _I64, _PP, _PP, _P, _P, _I64, _P,
                                                           _P]),
     "kvoff_stream_join_pipeline": (ctypes.c_int, [_P]),
-    "kvoff_stream_set_yield": (ctypes.c_int, [_P, _I32]),
     "kvoff_debug_bounded_wait": (ctypes.c_int, [_I64, _P]),
     "kvoff_copy_blocks": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _I64, _PI64, _I64, _PP, _I32,
                                          _I32, _I32, _P]),

@@ -216,15 +216,13 @@ class CPUBlockCache:
             self._restore_stream = (torch.cuda.Stream(pool.device) if split_streams
                                     else self._copy_stream)
             self._ready = torch.cuda.Event()  # re-recorded before each staged save
-            # Yield mode (kvoff_stream_set_yield) leaves the copy engine idle
-            # between blocks, so the engine's per-step input and sampled-token
-            # copies are not held behind a run of block transfers. It pays for
-            # BF16 blocks, whose transfers are twice as long; for FP8 blocks
-            # the gaps cost more than the stalls they remove. KVOFF_COPY_YIELD
-            # (0 or 1) overrides the choice.
-            if os.environ.get("KVOFF_COPY_YIELD", "0" if fp8 else "1") != "0":
-                for stream in {self._copy_stream, self._restore_stream}:
-                    ops.set_yield(pool.device, stream, True)
+            # Serial staged calls (staging_blocks = 1 at the C ABI) leave the
+            # copy engine idle while each block's kernel runs, so the engine's
+            # per-step input and sampled-token copies are not held behind a run
+            # of block transfers; KVOFF_COPY_YIELD=0 pipelines the kernels on
+            # the library's stream instead (more raw throughput, measured
+            # slower inside the engine).
+            self._serial = os.environ.get("KVOFF_COPY_YIELD", "1") != "0"
 
     # -- tensor parallelism ----------------------------------------------------
     #
@@ -394,17 +392,19 @@ class CPUBlockCache:
         chunk, index = self._locate(slot)
         return self._slabs[chunk][index], self._scale_slabs[chunk][index] if self._fp8 else None
 
-    def _stage(self, stream, blocks: int = 0) -> tuple[torch.Tensor, torch.Tensor | None]:
+    def _stage(self, stream, blocks: int = 0,
+               serial: bool = False) -> tuple[torch.Tensor, torch.Tensor | None]:
         """Per-stream device staging (FP8 payloads + scales, or raw blocks).
 
         Work on one stream runs in order, so reusing its staging is safe. It
         holds _staging_blocks blocks (2 by default: the staged FP8 calls then
         overlap the kernel of one block with the DMA of the previous one); a
         batched call grows it to min(blocks, _batch_staging_blocks) so a run of
-        blocks drains in few, large DMA copies. A replaced buffer is released
-        in stream order, after every copy that used it.
+        blocks drains in few, large DMA copies. serial=True (the staged calls'
+        serial form) needs one block. A replaced buffer is released in stream
+        order, after every copy that used it.
         """
-        want = max(self._staging_blocks, min(blocks, self._batch_staging_blocks))
+        want = 1 if serial else max(self._staging_blocks, min(blocks, self._batch_staging_blocks))
         staged = self._staging.get(stream)
         if staged is None or staged[0].shape[0] < want:
             device = self._cache.device
@@ -498,7 +498,10 @@ class CPUBlockCache:
         with scale None) with raw handles, the cache's own geometry and no
         per-call tensor checks. wait_events and event are recorded
         torch.cuda.Events or None."""
-        staged_payload, staged_scale = self._stage(stream, len(block_ids))
+        staged_payload, staged_scale = self._stage(stream, len(block_ids), self._serial)
+        blocks = 1 if self._serial else staged_payload.shape[0]
+        if scale is not None:
+            blocks = min(blocks, staged_scale.shape[0])
         g = self._geometry if pool is self._cache else self._ops.geometry(pool)
         waits = [e.cuda_event for e in wait_events]
         handle = event.cuda_event if event is not None else 0
@@ -508,13 +511,12 @@ class CPUBlockCache:
         with guard:
             if scale is None:
                 self._ops._copy_staged_ev(save, g, pool.data_ptr(), block_ids, payload,
-                                          staged_payload.data_ptr(), staged_payload.shape[0],
-                                          stream.cuda_stream, waits, handle)
+                                          staged_payload.data_ptr(), blocks, stream.cuda_stream,
+                                          waits, handle)
             else:
                 self._ops._fp8_staged_ev(save, g, pool.data_ptr(), block_ids, payload, scale,
                                          staged_payload.data_ptr(), staged_scale.data_ptr(),
-                                         min(staged_payload.shape[0], staged_scale.shape[0]),
-                                         stream.cuda_stream, waits, handle)
+                                         blocks, stream.cuda_stream, waits, handle)
 
     def _restore_slots(self, slots, block_ids, stream) -> torch.cuda.Event:
         """Restore slots into pool blocks on `stream`; returns the done event.

@@ -239,13 +239,6 @@ def join_pipeline(device, stream=None) -> None:
         _lib.call("kvoff_stream_join_pipeline", _stream(device, stream))
 
 
-def set_yield(device, stream, enable: bool) -> None:
-    """Yield mode of the staged calls on `stream` (kvoff_stream_set_yield)."""
-    device = torch.device(device)
-    with torch.cuda.device(device):
-        _lib.call("kvoff_stream_set_yield", _stream(device, stream), 1 if enable else 0)
-
-
 def copy_blocks(pool: torch.Tensor, block_ids, slot_ptrs, *, restore: bool = False,
                 method: int = COPY_ENGINE, stream=None, max_ctas: int = 0) -> None:
     """Byte-exact block moves pool <-> dense slots (BF16 passthrough)."""

@@ -140,11 +140,6 @@ def test_staged_block_copies_check_their_arguments_on_the_host():
     assert rc == _lib.KVOFF_EINVAL and "out of range" in _lib.last_error()
 
 
-def test_yield_mode_rejects_values_other_than_zero_and_one():
-    assert _lib.lib().kvoff_stream_set_yield(None, 2) == _lib.KVOFF_EINVAL
-    assert "0 or 1" in _lib.last_error()
-
-
 def test_ops_rejects_events_that_were_never_recorded():
     from kvoff import ops
 

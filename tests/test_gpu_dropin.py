@@ -186,13 +186,15 @@ def test_block_reuse_waits_for_pending_save(cuda):
     assert torch.equal(payload.view(torch.uint8).reshape(-1), expected.reshape(-1))
 
 
-def test_fp8_block_reuse_waits_for_the_read_not_the_drain(cuda):
-    """Staged FP8: before_block_reuse waits for the quantize kernel alone.
+def test_fp8_block_reuse_waits_for_the_read_not_the_drain(cuda, monkeypatch):
+    """Staged FP8 (pipelined: KVOFF_COPY_YIELD=0): before_block_reuse waits for
+    the quantize kernel alone.
 
     The copy stream sleeps before the save, so the drain to host is still
     queued when the block is overwritten; the slot must still hold the block
     as it was when saved.
     """
+    monkeypatch.setenv("KVOFF_COPY_YIELD", "0")
     engine = FakeEngine(finite_pool(SHAPES[1], cuda, seed=2))
     m = engine.manager
     key = m.publish(3)
@@ -217,9 +219,11 @@ def test_fp8_block_reuse_waits_for_the_read_not_the_drain(cuda):
     assert np.array_equal(bits_u16(entry.scale), want_s[0])
 
 
-def test_bf16_staged_block_reuse_waits_for_the_gather_not_the_drain(cuda):
-    """Staged BF16: before_block_reuse waits for the gather kernel alone, as
-    for staged FP8; the slot still receives the block as it was when saved."""
+def test_bf16_staged_block_reuse_waits_for_the_gather_not_the_drain(cuda, monkeypatch):
+    """Staged BF16 (pipelined: KVOFF_COPY_YIELD=0): before_block_reuse waits for the
+    gather kernel alone, as for staged FP8; the slot still receives the block
+    as it was when saved."""
+    monkeypatch.setenv("KVOFF_COPY_YIELD", "0")
     engine = FakeEngine(arbitrary_pool(SHAPES[1], cuda))
     m = engine.manager
     key = m.publish(3)

@@ -201,23 +201,14 @@ def test_fp8_staged_and_mapped_pinned_slots(cuda):
     assert np.array_equal(u16(pool), bits)
 
 
-@pytest.mark.parametrize("yielding", [False, True])
-def test_fp8_staged_pipeline_over_many_groups_and_calls(cuda, yielding):
+@pytest.mark.parametrize("serial", [False, True])
+def test_fp8_staged_pipeline_over_many_groups_and_calls(cuda, serial):
     """Staging of 4 blocks runs as a two-half pipeline (kernels on a library
-    stream), with and without yield mode."""
-    from kvoff import ops
-
-    stream = torch.cuda.Stream(cuda)
-    ops.set_yield(cuda, stream, yielding)
-    try:
-        _fp8_staged_pipeline(cuda, stream)
-    finally:
-        ops.set_yield(cuda, stream, False)
-
-
-def _fp8_staged_pipeline(cuda, stream):
+    stream); staging_blocks = 1 runs the same calls serially on the stream."""
     from kvoff import ops
     from kvoff.slab import PinnedSlab
+
+    stream = torch.cuda.Stream(cuda)
 
     bits = special_pool(2, 12, 128, 8, 128, seed=6)
     pool = to_bf16(bits, cuda)
@@ -228,7 +219,7 @@ def _fp8_staged_pipeline(cuda, stream):
                for i in range(7)]
     scale = [slab.view(7 * g.fp8_payload_bytes + i * g.fp8_scale_bytes, (g.fp8_scale_bytes,),
                        torch.uint8) for i in range(7)]
-    staging = empty_slots(4, g, cuda)
+    staging = empty_slots(1 if serial else 4, g, cuda)
     ids = [11, 3, 7, 0, 5, 9, 1]
     want_p, want_s = oracle.fp8_save_blocks(bits, ids)
     for chunk in ([0, 1, 2, 3, 4], [5], [6]):  # one multi-group call, then two one-block calls
@@ -345,24 +336,12 @@ def test_bf16_passthrough_byte_exact(cuda, method, shape):
 
 @pytest.mark.parametrize("staging_blocks", [1, 2, 3, 8])
 @pytest.mark.parametrize("misaligned", [False, True])
-@pytest.mark.parametrize("yielding", [False, True])
-def test_bf16_staged_copies_byte_exact(cuda, staging_blocks, misaligned, yielding):
-    """kvoff_copy_blocks_staged: one and two-half staging, groups smaller than
-    the batch, back-to-back calls on one ring, a pool whose base is only
-    2-byte aligned (the SM-kernel fallback instead of TMA), with and without
-    yield mode."""
+def test_bf16_staged_copies_byte_exact(cuda, staging_blocks, misaligned):
+    """kvoff_copy_blocks_staged: serial (one-block staging) and two-half
+    pipelined staging, groups smaller than the batch, back-to-back calls on
+    one ring, and a pool whose base is only 2-byte aligned (the SM-kernel
+    fallback instead of TMA)."""
     from kvoff import device_error, ops
-
-    ops.set_yield(cuda, None, yielding)
-    try:
-        _bf16_staged_round_trip(cuda, staging_blocks, misaligned)
-    finally:
-        ops.set_yield(cuda, None, False)
-    assert device_error(0) == 0
-
-
-def _bf16_staged_round_trip(cuda, staging_blocks, misaligned):
-    from kvoff import ops
     from kvoff.slab import PinnedSlab
 
     shape = (2, 3, 9, 256, 2, 64)
@@ -391,6 +370,7 @@ def _bf16_staged_round_trip(cuda, staging_blocks, misaligned):
     ops.join_pipeline(cuda)
     torch.cuda.synchronize()
     assert np.array_equal(u16(pool), bits)
+    assert device_error(0) == 0
 
 
 def test_bounded_device_wait_reports_a_timeout_and_the_context_survives(cuda):
