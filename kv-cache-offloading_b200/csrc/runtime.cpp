@@ -1,5 +1,5 @@
 // Host runtime of libkvoff: error reporting, fault injection, pinned NUMA-local
-// host slabs and plain async copies.
+// host slabs, plain async copies and the staged calls' two-half pipelines.
 #include "runtime.h"
 
 #include <errno.h>
@@ -152,6 +152,14 @@ int pipe_for(cudaStream_t caller, const void* staging, Pipe** out) {
   Pipe* p = nullptr;
   KVOFF_TRY(pipe_get(caller, &p));
   if (p->staging != staging) {  // a new staging buffer starts a fresh ring
+    // The fresh ring drops the waits on the old ring's halves, so the caller
+    // first waits for every kernel already queued on aux. Torch hands out
+    // stream handles from a pool, so another user of the same handle may have
+    // left kernels there that still read its own staging.
+    if (p->staging != nullptr) {
+      KVOFF_TRY(cuda_status(cudaEventRecord(p->done, p->aux), "cudaEventRecord"));
+      KVOFF_TRY(cuda_status(cudaStreamWaitEvent(caller, p->done, 0), "cudaStreamWaitEvent"));
+    }
     p->staging = staging;
     p->freed_recorded[0] = p->freed_recorded[1] = false;
     p->next = 0;

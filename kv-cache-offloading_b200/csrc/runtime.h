@@ -69,7 +69,8 @@ struct Pipe {
 std::mutex& pipe_mutex();
 
 // The pipeline of (current device, caller); a new staging buffer starts a
-// fresh ring. Creates the stream and events on first use.
+// fresh ring, after `caller` waits for the kernels already queued on the
+// pipeline's stream. Creates the stream and events on first use.
 int pipe_for(cudaStream_t caller, const void* staging, Pipe** out);
 
 // Makes `caller` wait for everything its pipeline queued on the auxiliary
