@@ -569,7 +569,8 @@ def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, mai
     """FP8 save + restore of the step's blocks through the drop-in CPUBlockCache.
 
     per_block: one save_block / _copy_entry per block, the block manager's call
-    pattern; batched: one save_blocks and one _copy_entries per step. The step
+    pattern; batched: one save_blocks and one _copy_entries per step; staged_form:
+    whether the cache ran its staged calls serially (the default) or pipelined. The step
     joins both copy streams into the timing stream; each step discards the saved
     entries so that the next step saves them again.
     """
@@ -662,6 +663,8 @@ def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, mai
     out["restore_ms_per_block"] = {
         str(b): 1e3 * cache.measure_restore_s_per_block(repeats=max(1, 64 // b), batch=b)
         for b in SWEEP_BATCHES if b <= B}
+    # The drop-in's staged-call form: serial (default) or pipelined (KVOFF_COPY_YIELD=0).
+    out["staged_form"] = "serial" if cache._serial else "pipelined"
     cache.close()
     return out
 
