@@ -70,6 +70,7 @@ def test_bf16_round_trip_byte_exact(cuda, monkeypatch, method, shape):
     cache = engine.create_cpu_prefix_cache(2 * per_block(engine.pool), split_streams=True)
     assert cache.save_block(key)
     m.forget(key)
+    cache.before_block_reuse(1)  # the engine's protocol: the save must read block 1 first
     engine.pool.fill_(-7)
     target = cache.restore_block(key)
     cache.synchronize()
