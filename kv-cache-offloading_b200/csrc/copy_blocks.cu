@@ -379,11 +379,19 @@ int kvoff_copy_blocks_staged(void* pool, int64_t num_chunks, int64_t chunk_strid
     if (host_slots[i] == nullptr)
       return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: null slot at %lld", (long long)i);
   }
-  cudaPointerAttributes attr;
-  if (cudaPointerGetAttributes(&attr, staging) != cudaSuccess ||
-      attr.type != cudaMemoryTypeDevice) {
-    cudaGetLastError();
-    return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: staging must be device memory");
+  // The staging buffer must be device memory. A caller reuses one buffer for
+  // every call on a stream, so the driver query runs only when the buffer
+  // changes: it is kept off the per-block path, where a driver call can stall
+  // the host behind queued device work.
+  static thread_local const void* checked_staging = nullptr;
+  if (staging != checked_staging) {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, staging) != cudaSuccess ||
+        attr.type != cudaMemoryTypeDevice) {
+      cudaGetLastError();
+      return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: staging must be device memory");
+    }
+    checked_staging = staging;
   }
   const CopyGeometry g{num_chunks, chunk_stride_bytes, block_stride_bytes, chunk_bytes};
   const int64_t bb = num_chunks * chunk_bytes;  // one dense block in staging and in a slot

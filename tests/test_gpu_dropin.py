@@ -187,13 +187,41 @@ def test_block_reuse_waits_for_pending_save(cuda):
     assert torch.equal(payload.view(torch.uint8).reshape(-1), expected.reshape(-1))
 
 
+def _reuse_while_draining(engine, cache, key, block):
+    """Save `block` while the copy stream sleeps, then reuse it (before_block_reuse
+    and the next writer). Returns (ms to the writer's end, ms to the drain's end),
+    both from the start of the sleep, on device clocks. The sequence runs once
+    untimed first: a first launch in a process can synchronize implicitly while
+    its kernel module loads, which would hide what the ordering alone does."""
+    original = engine.pool[:, :, block].clone()
+    for timed in (False, True):
+        slept = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(cache._copy_stream):
+            slept.record()
+            if timed:
+                torch.cuda._sleep(5 * SLEEP_CYCLES)
+        assert cache.save_block(key)
+        drained = torch.cuda.Event(enable_timing=True)
+        drained.record(cache._copy_stream)  # after the drain to host
+        cache.before_block_reuse(block)
+        engine.pool[:, :, block].fill_(5)  # the block's next writer
+        written = torch.cuda.Event(enable_timing=True)
+        written.record(torch.cuda.current_stream(engine.pool.device))
+        cache.synchronize()
+        torch.cuda.synchronize()
+        if not timed:
+            assert cache.discard(key)
+            engine.pool[:, :, block].copy_(original)
+    return slept.elapsed_time(written), slept.elapsed_time(drained)
+
+
 def test_fp8_block_reuse_waits_for_the_read_not_the_drain(cuda, monkeypatch):
     """Staged FP8 (pipelined: KVOFF_COPY_YIELD=0): before_block_reuse waits for
     the quantize kernel alone.
 
     The copy stream sleeps before the save, so the drain to host is still
-    queued when the block is overwritten; the slot must still hold the block
-    as it was when saved.
+    queued when the block is overwritten; the writer must finish long before
+    the drain, and the slot must still hold the block as it was when saved.
     """
     monkeypatch.setenv("KVOFF_COPY_YIELD", "0")
     engine = FakeEngine(finite_pool(SHAPES[1], cuda, seed=2))
@@ -203,17 +231,8 @@ def test_fp8_block_reuse_waits_for_the_read_not_the_drain(cuda, monkeypatch):
     cache = engine.create_cpu_prefix_cache(per_block(engine.pool), fp8=True,
                                            split_streams=True, preallocate=True)
     assert cache._modes["fp8_save"] == "staged"
-    assert cache.save_block(key)  # allocates the staging buffers outside the timed part
-    cache.synchronize()
-    assert cache.discard(key)
-    with torch.cuda.stream(cache._copy_stream):
-        torch.cuda._sleep(5 * SLEEP_CYCLES)
-    assert cache.save_block(key)
-    cache.before_block_reuse(3)
-    engine.pool[:, :, 3].fill_(5)  # the block's next writer
-    torch.cuda.current_stream(cuda).synchronize()
-    assert not cache._copy_stream.query()  # the drain has not finished
-    cache.synchronize()
+    write_ms, drain_ms = _reuse_while_draining(engine, cache, key, 3)
+    assert write_ms < drain_ms / 2, (write_ms, drain_ms)
     want_p, want_s = oracle.fp8_save_blocks(source, [3])
     entry = cache._entries[key]
     assert np.array_equal(entry.kv.view(torch.uint8).numpy(), want_p[0])
@@ -232,17 +251,8 @@ def test_bf16_staged_block_reuse_waits_for_the_gather_not_the_drain(cuda, monkey
     cache = engine.create_cpu_prefix_cache(per_block(engine.pool), split_streams=True,
                                            preallocate=True)
     assert cache._modes["bf16_save"] == "staged"
-    assert cache.save_block(key)  # allocates the staging buffers outside the timed part
-    cache.synchronize()
-    assert cache.discard(key)
-    with torch.cuda.stream(cache._copy_stream):
-        torch.cuda._sleep(5 * SLEEP_CYCLES)
-    assert cache.save_block(key)
-    cache.before_block_reuse(3)
-    engine.pool[:, :, 3].fill_(5)  # the block's next writer
-    torch.cuda.current_stream(cuda).synchronize()
-    assert not cache._copy_stream.query()  # the drain has not finished
-    cache.synchronize()
+    write_ms, drain_ms = _reuse_while_draining(engine, cache, key, 3)
+    assert write_ms < drain_ms / 2, (write_ms, drain_ms)
     payload, _ = cache._slot_view(cache._entries[key].slot)
     assert torch.equal(payload.view(torch.uint8).reshape(-1), expected.reshape(-1))
 
