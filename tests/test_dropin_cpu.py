@@ -326,3 +326,20 @@ def test_batched_save_is_all_or_nothing():
     assert len(cache) == 0
     assert cache.save_blocks(keys[:2]) == [True, True]
     assert cache.bytes_used == 2 * cache.block_bytes
+
+
+def test_copy_method_defaults_and_overrides(monkeypatch):
+    """CUDA pools default to the staged calls for both payload kinds; the
+    KVOFF_* variables choose another method, and unknown names are rejected
+    before any cache is built."""
+    for key in ("KVOFF_FP8_SAVE", "KVOFF_FP8_RESTORE", "KVOFF_BF16_SAVE", "KVOFF_BF16_RESTORE"):
+        monkeypatch.delenv(key, raising=False)
+    assert cpc._transfer_modes() == {"fp8_save": "staged", "fp8_restore": "staged",
+                                     "bf16_save": "staged", "bf16_restore": "staged"}
+    monkeypatch.setenv("KVOFF_BF16_RESTORE", "engine")
+    monkeypatch.setenv("KVOFF_FP8_SAVE", "mapped")
+    modes = cpc._transfer_modes()
+    assert modes["bf16_restore"] == "engine" and modes["fp8_save"] == "mapped"
+    monkeypatch.setenv("KVOFF_BF16_SAVE", "dma")
+    with pytest.raises(ValueError, match="KVOFF_BF16_SAVE"):
+        cpc._transfer_modes()
