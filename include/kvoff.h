@@ -167,8 +167,10 @@ KVOFF_API int kvoff_fp8_save_blocks_staged_ev(const void* pool, int64_t num_chun
  * loads the library until the process exits) and calls no allocator. Blocks
  * larger than the scratch are processed in pieces of whole (K/V, layer)
  * chunks; a chunk whose payload (rounded up to 256 bytes) plus scales exceeds
- * 16 MiB is rejected with KVOFF_EINVAL. The first call on each device looks up
- * the scratch's device address, so make that first call before any stream
+ * 16 MiB is rejected with KVOFF_EINVAL. The pool's device must be the current
+ * device (the scratch used is the current device's; another device's pool is
+ * rejected with KVOFF_EINVAL). The first call on each device looks up the
+ * scratch's device address, so make that first call before any stream
  * capture. All calls share the one scratch array and leave their data in it:
  * calls that may overlap on the GPU (different streams, or different host
  * threads) race and must be serialized by the caller. No counterpart in the

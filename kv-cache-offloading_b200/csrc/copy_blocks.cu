@@ -379,20 +379,12 @@ int kvoff_copy_blocks_staged(void* pool, int64_t num_chunks, int64_t chunk_strid
     if (host_slots[i] == nullptr)
       return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: null slot at %lld", (long long)i);
   }
-  // The staging buffer must be device memory. A caller reuses one buffer for
-  // every call on a stream, so the driver query runs only when the buffer
-  // changes: it is kept off the per-block path, where a driver call can stall
-  // the host behind queued device work.
-  static thread_local const void* checked_staging = nullptr;
-  if (staging != checked_staging) {
-    cudaPointerAttributes attr;
-    if (cudaPointerGetAttributes(&attr, staging) != cudaSuccess ||
-        attr.type != cudaMemoryTypeDevice) {
-      cudaGetLastError();
-      return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: staging must be device memory");
-    }
-    checked_staging = staging;
-  }
+  // The staging buffer must be device memory (the query is remembered per
+  // buffer, so it runs once for each staging buffer a caller reuses).
+  int staging_device = -1;
+  KVOFF_TRY(device_memory_of(staging, &staging_device));
+  if (staging_device < 0)
+    return fail(KVOFF_EINVAL, "kvoff_copy_blocks_staged: staging must be device memory");
   const CopyGeometry g{num_chunks, chunk_stride_bytes, block_stride_bytes, chunk_bytes};
   const int64_t bb = num_chunks * chunk_bytes;  // one dense block in staging and in a slot
   // TMA where every address and stride allows 16-byte bulk copies, else the SM kernel.

@@ -707,6 +707,16 @@ extern "C" int kvoff_fp8_save_blocks_staged_noalloc(
                 "of scratch, more than the %lld-byte maximum",
                 (long long)((chunk_payload + 255) / 256 * 256 + chunk_scale),
                 (long long)kNoAllocScratchBytes);
+  // The scratch address belongs to the current device, so the pool (and the
+  // stream) must be on that device too.
+  int current = 0, pool_device = -1;
+  KVOFF_TRY(cuda_status(cudaGetDevice(&current), "cudaGetDevice"));
+  KVOFF_TRY(device_memory_of(pool, &pool_device));
+  if (pool_device != current)
+    return fail(KVOFF_EINVAL,
+                "kvoff_fp8_save_blocks_staged_noalloc: the pool is not device memory of the "
+                "current device %d; make the pool's device current",
+                current);
   void* scratch = nullptr;
   KVOFF_TRY(noalloc_scratch(&scratch));
   cudaStream_t s = static_cast<cudaStream_t>(stream);

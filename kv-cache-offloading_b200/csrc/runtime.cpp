@@ -108,6 +108,35 @@ int64_t streaming_grid(int64_t units, int64_t per_cta, int32_t max_ctas) {
   return grid < 1 ? 1 : grid;
 }
 
+int device_memory_of(const void* p, int* device) {
+  struct Seen {
+    const void* p;
+    int device;
+  };
+  constexpr int kSeen = 8;
+  static thread_local Seen seen[kSeen] = {};
+  static thread_local int next = 0;
+  if (p != nullptr)
+    for (const Seen& s : seen)
+      if (s.p == p) {
+        *device = s.device;
+        return KVOFF_OK;
+      }
+  int dev = -1;
+  cudaPointerAttributes attr;
+  if (p != nullptr && cudaPointerGetAttributes(&attr, p) == cudaSuccess &&
+      attr.type == cudaMemoryTypeDevice)
+    dev = attr.device;
+  else
+    cudaGetLastError();  // clears the error a plain host pointer leaves behind
+  if (p != nullptr) {
+    seen[next] = Seen{p, dev};
+    next = (next + 1) % kSeen;
+  }
+  *device = dev;
+  return KVOFF_OK;
+}
+
 int copy_runs(void* const* dst, void* const* src, int64_t n, int64_t bytes, cudaStream_t s,
               const char* what) {
   for (int64_t i = 0; i < n;) {

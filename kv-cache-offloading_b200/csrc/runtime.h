@@ -41,6 +41,14 @@ int64_t grid_for(int64_t units, const void* kernel, int threads, size_t smem, in
 // busier than a persistent grid of resident CTAs.
 int64_t streaming_grid(int64_t units, int64_t per_cta, int32_t max_ctas);
 
+// Owning device of `p` when it is device memory, else -1, in *device. The
+// answer comes from cudaPointerGetAttributes and is remembered per thread for
+// the last few pointers asked about: callers pass the same pool and staging
+// buffers on every call, so the driver query stays off the per-block path.
+// A remembered answer outlives a free of that buffer; the checks it serves
+// only catch a host pointer, or another device's buffer, passed by mistake.
+int device_memory_of(const void* p, int* device);
+
 // Copies dst[i] <- src[i] of `bytes` each, for i < n, merged into one
 // cudaMemcpyAsync per run of entries that are adjacent on both sides (slots of
 // a slab are consecutive, and so is a staging buffer), so a group of blocks

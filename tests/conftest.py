@@ -6,6 +6,7 @@ device and call the hot path through libkvoff's C ABI.
 
 from __future__ import annotations
 
+import gc
 import sys
 from pathlib import Path
 
@@ -40,3 +41,18 @@ def cuda():
     if not torch.cuda.is_available():
         pytest.skip("CUDA device unavailable")
     return torch.device("cuda", 0)
+
+
+@pytest.fixture(autouse=True)
+def _release_test_garbage():
+    """Collect each test's garbage when it ends.
+
+    Caches that sit in reference cycles (an automatic cache and its block
+    manager, a cache whose copy methods a test wrapped) keep their pinned
+    slabs until the cyclic garbage collector runs. Unpinning a slab
+    (cudaHostUnregister) waits for the device, so a collection that happened
+    to run inside a later test's timed region would stall its host thread
+    behind that test's queued work. Collecting here frees them between tests.
+    """
+    yield
+    gc.collect()

@@ -11,6 +11,8 @@ Failures are injected on the host through kvoff_debug_fail_next.
 
 from __future__ import annotations
 
+import gc
+
 import numpy as np
 import pytest
 import torch
@@ -192,26 +194,36 @@ def _reuse_while_draining(engine, cache, key, block):
     and the next writer). Returns (ms to the writer's end, ms to the drain's end),
     both from the start of the sleep, on device clocks. The sequence runs once
     untimed first: a first launch in a process can synchronize implicitly while
-    its kernel module loads, which would hide what the ordering alone does."""
+    its kernel module loads, which would hide what the ordering alone does.
+
+    The garbage collector is off while the sequence is enqueued: a collection
+    there could free an earlier test's pinned slab, and unpinning waits for the
+    device (the sleep included), which would delay the writer's enqueue on the
+    host rather than its ordering on the device."""
     original = engine.pool[:, :, block].clone()
-    for timed in (False, True):
-        slept = torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(cache._copy_stream):
-            slept.record()
-            if timed:
-                torch.cuda._sleep(5 * SLEEP_CYCLES)
-        assert cache.save_block(key)
-        drained = torch.cuda.Event(enable_timing=True)
-        drained.record(cache._copy_stream)  # after the drain to host
-        cache.before_block_reuse(block)
-        engine.pool[:, :, block].fill_(5)  # the block's next writer
-        written = torch.cuda.Event(enable_timing=True)
-        written.record(torch.cuda.current_stream(engine.pool.device))
-        cache.synchronize()
-        torch.cuda.synchronize()
-        if not timed:
-            assert cache.discard(key)
-            engine.pool[:, :, block].copy_(original)
+    gc.collect()
+    gc.disable()
+    try:
+        for timed in (False, True):
+            slept = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(cache._copy_stream):
+                slept.record()
+                if timed:
+                    torch.cuda._sleep(5 * SLEEP_CYCLES)
+            assert cache.save_block(key)
+            drained = torch.cuda.Event(enable_timing=True)
+            drained.record(cache._copy_stream)  # after the drain to host
+            cache.before_block_reuse(block)
+            engine.pool[:, :, block].fill_(5)  # the block's next writer
+            written = torch.cuda.Event(enable_timing=True)
+            written.record(torch.cuda.current_stream(engine.pool.device))
+            cache.synchronize()
+            torch.cuda.synchronize()
+            if not timed:
+                assert cache.discard(key)
+                engine.pool[:, :, block].copy_(original)
+    finally:
+        gc.enable()
     return slept.elapsed_time(written), slept.elapsed_time(drained)
 
 

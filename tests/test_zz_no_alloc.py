@@ -85,3 +85,19 @@ def test_noalloc_save_rejects_chunks_larger_than_the_scratch():
         rows_per_chunk, 128, ids, 1, slot, slot, None)
     assert rc == _lib.KVOFF_EINVAL
     assert "maximum" in _lib.last_error()
+
+
+def test_noalloc_save_rejects_a_pool_off_the_current_device():
+    """The scratch used is the current device's, so a pool in host memory (or
+    on another device) is refused before anything is enqueued."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device unavailable")
+    torch.cuda.set_device(0)
+    pool = torch.zeros((2, 2, 2, 256, 1, 4), dtype=torch.bfloat16)  # host memory
+    chunks, cs, bst, nb, rpc, d = _geometry(pool)
+    slot = torch.empty(chunks * rpc * d, dtype=torch.uint8, pin_memory=True)
+    rc = _lib.lib().kvoff_fp8_save_blocks_staged_noalloc(
+        ctypes.c_void_p(pool.data_ptr()), chunks, cs, bst, nb, rpc, d, _lib.int64_array([0]), 1,
+        _lib.pointer_array([slot.data_ptr()]), _lib.pointer_array([slot.data_ptr()]), None)
+    assert rc == _lib.KVOFF_EINVAL
+    assert "current device" in _lib.last_error()
