@@ -18,9 +18,19 @@ Both are GB/s of KV processed, counted as bf16 bytes for saves plus restores;
 tokens/s counts block_size tokens per block moved.
 
 `--impl reference` times the reference algorithm on the host cores instead
-(the C oracle port of the reference's CPU-pool save / restore path).
+(the C oracle port of the reference's CPU-pool save / restore path), with all
+the host threads of the process's affinity set.
 Multi-GPU (torchrun): every rank runs the workload on its own GPU and slab
-(KV-head sharding needs no collective); time is the max over ranks.
+(KV-head sharding needs no collective); time is the max over ranks. At N > 1
+the line also carries `config4`: BASELINE config 4 on the same ranks (each
+rank's KV-head shard, 512-block restore || 512-block save), after config 2.
+
+At N=1 the line also reports the single-GPU characterizations: the staged /
+mapped and BF16 mode sweep, the staging-depth and issue-order sweep of the e2e
+step, the BF16 copy kernels, store_kvcache against the reference's own Triton
+kernel, KV handoff, and the drop-in cache beside the reference's own
+CPUBlockCache on the same GPU (both loaded from the reference's installed copy
+under baseline/_ref when it is present).
 """
 
 from __future__ import annotations
@@ -48,6 +58,8 @@ METRIC = "KV restore+save GB/s (FP8, bf16-equivalent bytes)"
 # kernel on 8 config-2 blocks (profiles/fp8_save_kernel_config2.md), per byte of
 # bf16 block read; traffic scales with blocks because each is read and written once.
 SAVE_KERNEL_DRAM_BYTES_PER_BF16_BYTE = (302_021_632 + 100_535_552) / (8 * 37_748_736)
+TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one 8-block launch "
+                  "(profiles/fp8_save_kernel_config2.md), scaled by blocks per launch")
 
 
 @dataclass(frozen=True)
@@ -123,6 +135,10 @@ def parse_args():
     p.add_argument("--no-dropin", action="store_true",
                    help="skip the per-block vs batched CPUBlockCache measurement")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
+    p.add_argument("--staging-blocks", type=int, default=16,
+                   help="FP8 staging depth of the e2e step before the arrangement sweep")
+    p.add_argument("--no-config4", action="store_true",
+                   help="at N > 1, skip the extra config-4 (KV-head sharded) measurement")
     args = p.parse_args()
     if args.warmup < 3:
         p.error("--warmup must be >= 3")
@@ -236,14 +252,26 @@ def host_cpu() -> dict:
             "logical_cpus": os.cpu_count()}
 
 
+def host_threads() -> int:
+    """Host CPUs this process may run on (its affinity set).
+
+    torchrun exports OMP_NUM_THREADS=1 to every rank; the host-core baseline
+    sets its thread count from the affinity set instead, so that it uses the
+    cores the job holds whatever the launcher exported.
+    """
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, os.cpu_count() or 1)
+
+
 def cpu_sample(w: Workload, seconds: float, threads: int | None = None) -> dict:
     """Save + restore FP8 blocks of the workload's shape on the host cores."""
     import numpy as np
 
     from oracle import oracle
 
-    if threads:
-        oracle.set_threads(threads)
+    oracle.set_threads(threads or host_threads())
     cores = oracle.max_threads()
     if _CPU_STATE.get("workload") != w:  # 4 blocks: 2 saved + 2 restored per iteration
         rng = np.random.default_rng(0)
@@ -283,6 +311,7 @@ def torch_ops_sample(w: Workload, seconds: float) -> dict:
 
     from kvoff.cpu_prefix_cache import fp8_dequantize, fp8_quantize
 
+    torch.set_num_threads(host_threads())
     bits = _CPU_STATE["pool"]
     pool = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16)
     shape = (2, w.layers, w.block_size, w.heads, w.head_dim)
@@ -305,10 +334,11 @@ def run_reference(args) -> None:
     if rank != 0:
         return  # rank 0 alone runs the host-core baseline
     w = make_workload(args, world)
+    threads = host_threads()
     per_step = max(0.5, min(5.0, 120.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
-        cpu_sample(w, per_step / 4)
-    samples = [cpu_sample(w, per_step) for _ in range(args.steps)]
+        cpu_sample(w, per_step / 4, threads)
+    samples = [cpu_sample(w, per_step, threads) for _ in range(args.steps)]
     value = statistics.mean(s["value"] for s in samples)
     emit({"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
           "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -319,7 +349,12 @@ def run_reference(args) -> None:
                      "pool_blocks": w.num_blocks, "sample_blocks_per_step": 4,
                      "note": "host-core sample of the workload: each step saves 2 and "
                              "restores 2 blocks of the same shape (GB/s does not depend on "
-                             "the batch on the host)"},
+                             "the batch on the host)",
+                     "basis": "aggregate: the reference's CPU tier runs on the host's cores, "
+                              "which serve every GPU of the job, so its whole-job throughput "
+                              "is one sample on all the cores the job holds (the affinity "
+                              "set, not the launcher's OMP_NUM_THREADS)",
+                     "value_per_gpu": value / world},
           "cpu_baseline": {"value": value, "unit": "GB/s", "cores": samples[0]["cores"],
                            "kind": "port", "sample": samples[0]["sample"],
                            "host": samples[0]["host"]},
@@ -422,6 +457,7 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
     }
     per_step = w.layers * tokens * (4 * kv_width * 2 + 4)
     out = {"tokens": tokens, "layers": w.layers, "algorithmic_bytes_per_step": per_step}
+    ref_store = reference_store_kvcache()
     stream = torch.cuda.current_stream(device)
     bad = torch.zeros(1, dtype=torch.int32, device=device)
     for pattern, slots in patterns.items():
@@ -441,32 +477,60 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
                 caches[0, layer].view(-1, kv_width)[idx] = keys[layer].reshape(tokens, -1)[valid]
                 caches[1, layer].view(-1, kv_width)[idx] = values[layer].reshape(tokens, -1)[valid]
 
+        def reference(slots=slots):  # the reference's Triton kernel, unchanged
+            for layer in range(w.layers):
+                ref_store(keys[layer], values[layer], caches[0, layer], caches[1, layer], slots)
+
         # Eager: one Python call per layer, as in a prefill forward. Graph: the
         # same 36 launches captured in a CUDA graph, which isolates the kernel
         # from the host launch path (decode steps run this way under the
         # engine's graphs).
-        side = torch.cuda.Stream(device)
-        side.wait_stream(stream)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(side):
-            ours()
-            with torch.cuda.graph(graph, stream=side):
-                ours()
-        stream.wait_stream(side)
+        def captured(fn):
+            side = torch.cuda.Stream(device)
+            side.wait_stream(stream)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(side):
+                fn()  # first call outside the capture (Triton compiles here)
+                with torch.cuda.graph(graph, stream=side):
+                    fn()
+            stream.wait_stream(side)
+            return graph
+
+        arms = [("kvoff", ours)] + ([("reference_triton", reference)] if callable(ref_store)
+                                    else [])
         res = {}
-        for name, fn in (("kvoff_eager", ours), ("kvoff_graph", graph.replay),
-                         ("torch_index_put", torch_scatter)):
-            ms = Timer(torch, stream, 1).run(fn, args.steps, args.warmup) / args.steps
-            res[name] = {"ms_per_step": ms, "GBps": per_step / (ms / 1e3) / 1e9,
-                         "us_per_launch": 1e3 * ms / w.layers}
-        res["kvoff_graph"]["frac_of_hbm_peak"] = res["kvoff_graph"]["GBps"] / hbm_peak
-        del graph
+        for arm, fn in arms:
+            graph = captured(fn)
+            for mode, run in (("eager", fn), ("graph", graph.replay)):
+                ms = Timer(torch, stream, 1).run(run, args.steps, args.warmup) / args.steps
+                res[f"{arm}_{mode}"] = {"ms_per_step": ms, "GBps": per_step / (ms / 1e3) / 1e9,
+                                        "us_per_launch": 1e3 * ms / w.layers,
+                                        "frac_of_hbm_peak": per_step / (ms / 1e3) / 1e9
+                                        / hbm_peak}
+            del graph
+        ms = Timer(torch, stream, 1).run(torch_scatter, args.steps, args.warmup) / args.steps
+        res["torch_index_put"] = {"ms_per_step": ms, "GBps": per_step / (ms / 1e3) / 1e9,
+                                  "us_per_launch": 1e3 * ms / w.layers}
+        if not callable(ref_store):
+            res["reference_triton"] = {"unavailable": str(ref_store)[:200]}
         ops.store_kvcache(keys[0], values[0], caches[0, 0], caches[1, 0], slots, bad_slots=bad)
         out[pattern] = res
     torch.cuda.synchronize()
     out["bad_slots"] = int(bad.item())
     del keys, values, qkv
     return out
+
+
+def reference_store_kvcache():
+    """The reference's store_kvcache (nanovllm/layers/attention.py:10-40: its
+    Triton store_kvcache_kernel and launcher) from its installed copy, or the
+    reason it cannot run here."""
+    try:
+        if reference_module("nanovllm.utils.context") is None:
+            return "the reference's installed copy (baseline/_ref) is absent"
+        return reference_module("nanovllm.layers.attention").store_kvcache
+    except Exception as exc:  # e.g. its flash_attn or triton import failing
+        return f"{type(exc).__name__}: {exc}"
 
 
 def bf16_kernel_rates(torch, ops, w: Workload, pool, ids, hbm_peak: float, kernel_alone,
@@ -565,26 +629,72 @@ class _Block:
         self.block_id, self.hash, self.token_ids = block_id, -1, []
 
 
-def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, main) -> dict:
-    """FP8 save + restore of the step's blocks through the drop-in CPUBlockCache.
+REFERENCE_TREE = ROOT / "baseline" / "_ref" / "nanovllm_upstream" / "nanovllm"
 
-    per_block: one save_block / _copy_entry per block, the block manager's call
-    pattern; batched: one save_blocks and one _copy_entries per step; staged_form:
-    whether the cache ran its staged calls serially (the default) or pipelined. The step
-    joins both copy streams into the timing stream; each step discards the saved
-    entries so that the next step saves them again.
+
+def reference_module(name: str):
+    """A module of the reference's installed copy (baseline/_ref), loaded by
+    file path under its own package names without running the package's
+    __init__ (which imports the model stack). None when the copy is absent."""
+    import importlib.util
+    import types
+
+    relative = name.split(".", 1)[1].replace(".", "/") + ".py"
+    path = REFERENCE_TREE / relative
+    if not path.exists():
+        return None
+    if name in sys.modules:
+        return sys.modules[name]
+    parts = name.split(".")
+    for depth in range(1, len(parts)):  # namespace stand-ins for the packages
+        package = ".".join(parts[:depth])
+        if package not in sys.modules:
+            module = types.ModuleType(package)
+            module.__path__ = [str(REFERENCE_TREE.joinpath(*parts[1:depth]))]
+            sys.modules[package] = module
+    spec = importlib.util.spec_from_file_location(name, path)
+    module = importlib.util.module_from_spec(spec)
+    sys.modules[name] = module
+    spec.loader.exec_module(module)
+    return module
+
+
+def reference_cache_class():
+    """The reference's own CPUBlockCache (nanovllm/engine/cpu_prefix_cache.py)."""
+    for dep in ("nanovllm.sampling_params", "nanovllm.engine.sequence",
+                "nanovllm.engine.block_manager"):
+        if reference_module(dep) is None:
+            return None
+    module = reference_module("nanovllm.engine.cpu_prefix_cache")
+    return module.CPUBlockCache if module is not None else None
+
+
+def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, main,
+               cache_cls=None) -> dict:
+    """FP8 save + restore of the step's blocks through a CPUBlockCache.
+
+    cache_cls None is kvoff's drop-in; the reference's own class gives the
+    like-for-like comparator (same calls, same split streams and pinned slots,
+    its torch quantizer and copies). per_block: one save_block / _copy_entry per
+    block, the block manager's call pattern; batched (kvoff only): one
+    save_blocks and one _copy_entries per step; staged_form: whether kvoff ran
+    its staged calls serially (the default) or pipelined. The step joins both
+    copy streams into the timing stream; each step discards the saved entries
+    so that the next step saves them again.
     """
     from types import SimpleNamespace
 
-    from kvoff.cpu_prefix_cache import CPUBlockCache
+    ours = cache_cls is None
+    if ours:
+        from kvoff.cpu_prefix_cache import CPUBlockCache as cache_cls
 
     B = len(save_ids)
     blocks = [_Block(i) for i in range(w.num_blocks)]
     manager = SimpleNamespace(blocks=blocks, block_size=w.block_size, hash_to_block_id={},
                               _cpu_prefix_cache=None, admission_blocked=False)
     runner = SimpleNamespace(world_size=1, block_size=w.block_size, kv_cache=pool)
-    cache = CPUBlockCache(runner, manager, 2 * B * (w.fp8_block + 4096), split_streams=True,
-                          fp8=True, preallocate=True)
+    cache = cache_cls(runner, manager, 2 * B * (w.fp8_block + 4096), split_streams=True,
+                      fp8=True, preallocate=True)
 
     def publish(block_id: int, tag: int) -> int:
         h = 1_000_000 + tag
@@ -594,7 +704,8 @@ def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, mai
 
     saves = [publish(b, i) for i, b in enumerate(save_ids)]
     sources = [publish(b, B + i) for i, b in enumerate(restore_ids)]
-    cache.save_blocks(sources)
+    for h in sources:
+        cache.save_block(h)
     entries = [cache._entries[h] for h in sources]
     cache.synchronize()
 
@@ -617,9 +728,28 @@ def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, mai
         join()
 
     out = {}
-    for name, step in (("per_block", per_block), ("batched", batched)):
+    steps = [("per_block", per_block)] + ([("batched", batched)] if ours else [])
+    for name, step in steps:
         ms = timer.run(step, args.steps, args.warmup) / args.steps
         out[name] = 2 * B * w.bf16_block / (ms / 1e3) / 1e9
+    # Host time per call on the engine thread (the GPU work is asynchronous):
+    # 64 save_block calls, then 64 _copy_entry calls.
+    n = min(64, B)
+    main.synchronize()
+    t0 = time.perf_counter()
+    for h in saves[:n]:
+        cache.save_block(h)
+    t1 = time.perf_counter()
+    for e, b in zip(entries[:n], restore_ids[:n]):
+        cache._copy_entry(e, b, wait=False)
+    t2 = time.perf_counter()
+    join()
+    main.synchronize()
+    out["host_us_per_call"] = {"save_block": 1e6 * (t1 - t0) / n,
+                               "_copy_entry": 1e6 * (t2 - t1) / n}
+    if not ours:
+        cache.close()
+        return out
     # How long the compute stream waits before it may rewrite a block it just
     # saved (save_block, then before_block_reuse), against the wait for the
     # whole drain to host (the saved entry's event). Device time on the compute
@@ -645,21 +775,6 @@ def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, mai
             cache.discard(h)
     out.update({name: statistics.median(v) for name, v in waits.items()})
     # The hybrid planner's restore cost at the batch sizes admission restores.
-    # Host time per drop-in call (the engine thread's cost; the GPU work is
-    # asynchronous): 64 save_block calls, then 64 _copy_entry calls.
-    n = min(64, B)
-    main.synchronize()
-    t0 = time.perf_counter()
-    for h in saves[:n]:
-        cache.save_block(h)
-    t1 = time.perf_counter()
-    for e, b in zip(entries[:n], restore_ids[:n]):
-        cache._copy_entry(e, b, wait=False)
-    t2 = time.perf_counter()
-    join()
-    main.synchronize()
-    out["host_us_per_call"] = {"save_block": 1e6 * (t1 - t0) / n,
-                               "_copy_entry": 1e6 * (t2 - t1) / n}
     out["restore_ms_per_block"] = {
         str(b): 1e3 * cache.measure_restore_s_per_block(repeats=max(1, 64 // b), batch=b)
         for b in SWEEP_BATCHES if b <= B}
@@ -669,22 +784,16 @@ def dropin_e2e(torch, w: Workload, pool, save_ids, restore_ids, args, timer, mai
     return out
 
 
-def run_ours(args) -> None:
-    import numpy as np
+def init_ranks(args):
+    """One process per GPU: pick this rank's device and, for N > 1, join the
+    process group (used only for barriers and the max-over-ranks timing)."""
     import torch
-
-    from kvoff import ops
-    from kvoff.slab import PinnedSlab
 
     rank, local_rank, world = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device")
-    w = make_workload(args, world)
-    B = w.batch
-    if not 1 <= B <= w.num_blocks // 2:
-        raise SystemExit("the batch must be at most half the pool")
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
@@ -692,14 +801,62 @@ def run_ours(args) -> None:
 
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300),
                                              device_id=device)
+    return rank, local_rank, world, device
+
+
+def pcie_ceiling(torch, timer, concurrent, dev_buf, d2h_host, h2d_host, n_bytes: int,
+                 block: int) -> dict:
+    """Pinned cudaMemcpyAsync between `dev_buf` and two host ranges, per
+    direction and in duplex, in several arrangements: one copy per direction
+    issued D2H first or H2D first, one copy per block, and 4 MiB pieces. The
+    best duplex total is the link's ceiling for concurrent save and restore."""
+    cp = lambda d, s_: d.copy_(s_, non_blocking=True)  # noqa: E731
+    dev_d2h, dev_h2d = dev_buf[:n_bytes], dev_buf[n_bytes:2 * n_bytes]
+
+    def pieces(dst, src, size):
+        return lambda: [cp(dst[k:k + size], src[k:k + size]) for k in range(0, n_bytes, size)]
+
+    def rate(step, directions):
+        ms = timer.run(step, 5, 3) / 5
+        return directions * n_bytes / (ms / 1e3) / 1e9
+
+    d2h = lambda: cp(d2h_host, dev_d2h)  # noqa: E731
+    h2d = lambda: cp(dev_h2d, h2d_host)  # noqa: E731
+    out = {"d2h": rate(concurrent(d2h, lambda: None), 1),
+           "h2d": rate(concurrent(lambda: None, h2d), 1),
+           "duplex_total": rate(concurrent(d2h, h2d), 2),
+           "duplex_total_h2d_first": rate(concurrent(d2h, h2d, restore_first=True), 2),
+           "duplex_total_block_copies": rate(concurrent(pieces(d2h_host, dev_d2h, block),
+                                                        pieces(dev_h2d, h2d_host, block)), 2),
+           "duplex_total_4mib_copies": rate(concurrent(pieces(d2h_host, dev_d2h, 4 << 20),
+                                                       pieces(dev_h2d, h2d_host, 4 << 20)), 2),
+           "bytes_per_direction": n_bytes}
+    out["duplex_best"] = max(v for k, v in out.items() if k.startswith("duplex_total"))
+    return out
+
+
+def run_ours(args, w: Workload, rank: int, local_rank: int, world: int, device,
+             extras: bool) -> dict:
+    """Time `w` on this rank's GPU and return the bench line (rank 0 prints it).
+
+    extras adds the single-GPU characterizations (mode and staging sweeps, BF16
+    kernels, slot store, handoff, drop-in caches, torch-op comparison); the
+    multi-GPU runs time only the contract's steps.
+    """
+    import numpy as np
+    import torch
+
+    from kvoff import ops
+    from kvoff.slab import PinnedSlab
+
+    B = w.batch
+    if not 1 <= B <= w.num_blocks // 2:
+        raise SystemExit("the batch must be at most half the pool")
     main = torch.cuda.current_stream(device)
     save_stream = torch.cuda.Stream(device)
     restore_stream = torch.cuda.Stream(device)
     timer = Timer(torch, main, world)
-    # Per-GPU characterizations (mode sweep, drop-in cache, slot store, torch-op
-    # comparison) run at N=1; multi-GPU runs time only the contract's steps.
-    single = world == 1
-    sweep_batches = [b for b in SWEEP_BATCHES if b <= B] if single and not args.no_sweep else []
+    sweep_batches = [b for b in SWEEP_BATCHES if b <= B] if extras and not args.no_sweep else []
     bf16_batch = max(sweep_batches, default=0)
 
     pool = torch.empty((2, w.layers, w.num_blocks, w.block_size, w.heads, w.head_dim),
@@ -735,13 +892,14 @@ def run_ours(args) -> None:
     bf16_slots = [slab.view(fp8_bytes + i * w.bf16_block, (w.bf16_block,), torch.uint8)
                   for i in range(2 * bf16_batch)]
 
-    staging_blocks = min(B, 16)
-    staging = {name: (torch.empty((staging_blocks, w.fp8_payload), dtype=torch.uint8,
-                                  device=device),
-                      torch.empty((staging_blocks, w.fp8_scale), dtype=torch.uint8,
-                                  device=device))
-               for name in ("save", "restore")}
-    bf16_staging = {name: torch.empty((staging_blocks, w.bf16_block), dtype=torch.uint8,
+    def fp8_staging(blocks):
+        return {name: (torch.empty((blocks, w.fp8_payload), dtype=torch.uint8, device=device),
+                       torch.empty((blocks, w.fp8_scale), dtype=torch.uint8, device=device))
+                for name in ("save", "restore")}
+
+    staging_blocks = min(B, args.staging_blocks)
+    staging = fp8_staging(staging_blocks)
+    bf16_staging = {name: torch.empty((min(B, 16), w.bf16_block), dtype=torch.uint8,
                                       device=device) for name in ("save", "restore")} \
         if bf16_batch else {}
 
@@ -766,14 +924,14 @@ def run_ours(args) -> None:
     drp = [dev_src[0][i % ring].data_ptr() for i in range(B)]
     drs = [dev_src[1][i % ring].data_ptr() for i in range(B)]
 
-    def concurrent(save_fn, restore_fn):
+    def concurrent(save_fn, restore_fn, restore_first=False):
         def step():
             save_stream.wait_stream(main)
             restore_stream.wait_stream(main)
-            with torch.cuda.stream(save_stream):
-                save_fn()
-            with torch.cuda.stream(restore_stream):
-                restore_fn()
+            order = ((restore_stream, restore_fn), (save_stream, save_fn))
+            for stream, fn in (order if restore_first else order[::-1]):
+                with torch.cuda.stream(stream):
+                    fn()
             main.wait_stream(save_stream)
             main.wait_stream(restore_stream)
         return step
@@ -811,6 +969,7 @@ def run_ours(args) -> None:
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                 "frac": achieved / hbm_peak,
                 "traffic": SAVE_KERNEL_DRAM_BYTES_PER_BF16_BYTE * w.bf16_block * blocks_per_launch,
+                "traffic_source": TRAFFIC_SOURCE,
                 "kernel": f"fp8_save_kernel (gather + quantize, {int(blocks_per_launch)} blocks "
                           "per launch)",
                 "peak_source": peak_source, "algorithmic_bytes_per_block": w.kernel_bytes,
@@ -821,10 +980,11 @@ def run_ours(args) -> None:
 
     # ---- BF16 passthrough kernels, device-resident (pool <-> device slots) ----
     bf16_kernels = bf16_kernel_rates(torch, ops, w, pool, save_ids, hbm_peak, kernel_alone,
-                                     save_stream) if single else None
+                                     save_stream) if extras else None
 
     # ---- end to end through the C ABI with pinned host slots -----------------
-    def e2e_fns(batch, save_mode, restore_mode):
+    def e2e_fns(batch, save_mode, restore_mode, stage=None):
+        stage = stage or staging
         sids, rids = save_ids[:batch], restore_ids[:batch]
         ss, rs = save_slots[:batch], restore_slots[:batch]
         if save_mode == "mapped":
@@ -833,7 +993,7 @@ def run_ours(args) -> None:
         else:
             sp, sc = host_ptr(ss, 0), host_ptr(ss, 1)
             save = lambda: ops.save_fp8_staged(pool, sids, sp, sc,  # noqa: E731
-                                               *staging["save"], stream=save_stream)
+                                               *stage["save"], stream=save_stream)
         if restore_mode == "mapped":
             rp, rc = mapped_ptr(rs, 0), mapped_ptr(rs, 1)
             restore = lambda: ops.restore_fp8(pool, rids, rp, rc,  # noqa: E731
@@ -841,7 +1001,7 @@ def run_ours(args) -> None:
         else:
             rp, rc = host_ptr(rs, 0), host_ptr(rs, 1)
             restore = lambda: ops.restore_fp8_staged(pool, rids, rp, rc,  # noqa: E731
-                                                     *staging["restore"], stream=restore_stream)
+                                                     *stage["restore"], stream=restore_stream)
         return save, restore
 
     def bf16_fns(batch, method):
@@ -849,18 +1009,19 @@ def run_ours(args) -> None:
         ss, rs = bf16_slots[:batch], bf16_slots[bf16_batch:bf16_batch + batch]
         if method == "tma":
             st_s, st_r = bf16_staging["save"], bf16_staging["restore"]
+            depth = st_s.shape[0]
 
             def save():
-                for k in range(0, batch, staging_blocks):
-                    n = min(staging_blocks, batch - k)
+                for k in range(0, batch, depth):
+                    n = min(depth, batch - k)
                     ops.copy_blocks(pool, sids[k:k + n], [x.data_ptr() for x in st_s[:n]],
                                     method=ops.COPY_TMA, stream=save_stream)
                     ops.memcpy(ss[k].data_ptr(), st_s.data_ptr(), n * w.bf16_block,
                                device=device, stream=save_stream)
 
             def restore():
-                for k in range(0, batch, staging_blocks):
-                    n = min(staging_blocks, batch - k)
+                for k in range(0, batch, depth):
+                    n = min(depth, batch - k)
                     ops.memcpy(st_r.data_ptr(), rs[k].data_ptr(), n * w.bf16_block,
                                device=device, stream=restore_stream)
                     ops.copy_blocks(pool, rids[k:k + n], [x.data_ptr() for x in st_r[:n]],
@@ -917,9 +1078,29 @@ def run_ours(args) -> None:
     save_mode, restore_mode = max(combos, key=lambda c: duplex(*c)) if best else \
         ("staged", "staged")
 
+    # Staging depth of the staged calls (blocks per staging buffer; each half
+    # is drained by one cudaMemcpyAsync per run of consecutive slots), and the
+    # issue order of the two directions, at the full batch.
+    arrangement = {}
+    if extras and not args.no_sweep and "staged" in (save_mode, restore_mode):
+        for depth in sorted({8, 16, 32, 64} & set(range(2, B + 1)) | {staging_blocks}):
+            stage = staging if depth == staging_blocks else fp8_staging(depth)
+            save, restore = e2e_fns(B, save_mode, restore_mode, stage)
+            for first in ("save", "restore"):
+                arrangement[f"depth{depth}_{first}_first"] = rate(
+                    concurrent(save, restore, restore_first=first == "restore"), B, 2, **few)
+            del stage
+    best_arrangement = max(arrangement, key=arrangement.get) if arrangement else None
+    restore_first = bool(best_arrangement) and best_arrangement.endswith("restore_first")
+    if best_arrangement:
+        depth = int(best_arrangement[5:].split("_")[0])
+        if depth != staging_blocks:
+            staging_blocks, staging = depth, fp8_staging(depth)
+
     save, restore = e2e_fns(B, save_mode, restore_mode)
+    e2e_step = concurrent(save, restore, restore_first=restore_first)
     with ClockSampler(gpu_name) as clocks_e2e:
-        ms = timer.run(concurrent(save, restore), args.steps, args.warmup)
+        ms = timer.run(e2e_step, args.steps, args.warmup)
     e2e_ms = max_over_ranks(torch, ms, device) / args.steps
     e2e_value = world * 2 * B * w.bf16_block / (e2e_ms / 1e3) / 1e9
     groups = -(-B // max(1, staging_blocks // 2))
@@ -928,47 +1109,46 @@ def run_ours(args) -> None:
 
     # ---- prefill slot store (store_kvcache) ------------------------------------
     store = store_kvcache_bench(torch, w, pool, args, hbm_peak) \
-        if single and not args.no_store else None
+        if extras and not args.no_store else None
 
     # ---- KV handoff export / import of one sequence ---------------------------
     handoff = handoff_bench(torch, w, pool, args) \
-        if single and not args.no_handoff and w.num_blocks >= 64 else None
+        if extras and not args.no_handoff and w.num_blocks >= 64 else None
 
-    # ---- through the drop-in CPUBlockCache: per-block calls vs batched calls ----
-    dropin = dropin_e2e(torch, w, pool, save_ids, restore_ids, args, timer, main) \
-        if single and w.batch <= 256 and not args.no_dropin else None
+    # ---- through drop-in caches: kvoff's (per-block and batched calls) and the
+    # reference's own CPUBlockCache on the same GPU (like for like) -------------
+    dropin = None
+    if extras and w.batch <= 256 and not args.no_dropin:
+        dropin = dropin_e2e(torch, w, pool, save_ids, restore_ids, args, timer, main)
+        try:
+            stock_cls = reference_cache_class()
+            dropin["stock"] = (dropin_e2e(torch, w, pool, save_ids, restore_ids, args, timer,
+                                          main, cache_cls=stock_cls) if stock_cls is not None
+                               else {"unavailable": "the reference's installed copy "
+                                                    "(baseline/_ref) is absent"})
+        except Exception as exc:  # context only; never fails the bench
+            dropin["stock"] = {"error": f"{type(exc).__name__}: {str(exc)[:200]}"}
 
     # ---- PCIe ceiling: pinned memcpy per direction and duplex -------------------
+    # The slab's pages (mmap + cudaHostRegister, kvoff_host_alloc) and, beside
+    # them, pages from cudaHostAlloc (torch's pinned allocator); every rank
+    # copies at once, so at N > 1 this is the host's shared ceiling.
     blocks = min(B, 64, max(1, int(2.5e9 // w.fp8_block)))
     n_bytes = blocks * w.fp8_block
     dev_buf = torch.empty(2 * n_bytes, dtype=torch.uint8, device=device)
-    h_d2h, h_h2d = slab.bytes[:n_bytes], slab.bytes[n_bytes:2 * n_bytes]
-    cp = lambda d, s_: d.copy_(s_, non_blocking=True)  # noqa: E731
-
-    def chunked(dst, src):
-        return lambda: [cp(dst[k * w.fp8_block:(k + 1) * w.fp8_block],
-                           src[k * w.fp8_block:(k + 1) * w.fp8_block]) for k in range(blocks)]
-
-    def memcpy_rate(step, directions):
-        ms = timer.run(step, 5, 3) / 5
-        return directions * n_bytes / (ms / 1e3) / 1e9
-
-    d2h = lambda: cp(h_d2h, dev_buf[:n_bytes])  # noqa: E731
-    h2d = lambda: cp(dev_buf[n_bytes:], h_h2d)  # noqa: E731
-    ceiling = {"d2h": memcpy_rate(concurrent(d2h, lambda: None), 1),
-               "h2d": memcpy_rate(concurrent(lambda: None, h2d), 1),
-               "duplex_total": memcpy_rate(concurrent(d2h, h2d), 2),
-               "duplex_total_block_copies": memcpy_rate(
-                   concurrent(chunked(h_d2h, dev_buf[:n_bytes]),
-                              chunked(dev_buf[n_bytes:], h_h2d)), 2),
-               "bytes_per_copy": n_bytes}
-    del dev_buf
+    ceiling = pcie_ceiling(torch, timer, concurrent, dev_buf, slab.bytes[:n_bytes],
+                           slab.bytes[n_bytes:2 * n_bytes], n_bytes, w.fp8_block)
+    host_alloc = torch.empty(2 * n_bytes, dtype=torch.uint8, pin_memory=True)
+    ceiling["cuda_host_alloc"] = pcie_ceiling(torch, timer, concurrent, dev_buf,
+                                              host_alloc[:n_bytes], host_alloc[n_bytes:],
+                                              n_bytes, w.fp8_block)
+    del dev_buf, host_alloc
     pcie_per_dir = B * w.fp8_block / (e2e_ms / 1e3) / 1e9
 
     # ---- the reference's device path (torch ops) for context ------------------
     ref_gpu = None
     try:
-        if not single:
+        if not extras:
             raise StopIteration  # measured at N=1 only
         from kvoff.cpu_prefix_cache import fp8_dequantize, fp8_quantize
 
@@ -989,12 +1169,7 @@ def run_ours(args) -> None:
     except Exception as exc:  # context only; never fails the bench
         ref_gpu = {"error": str(exc)[:200]}
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_sample(w, args.cpu_seconds)
-        cpu["torch_ops_cpu"] = torch_ops_sample(w, min(5.0, args.cpu_seconds))
-
-    line = {
+    return {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -1002,6 +1177,7 @@ def run_ours(args) -> None:
         "config": {"workload": w.describe(), "batch_blocks": B, "pool_blocks": w.num_blocks,
                    "pool_bytes": pool.numel() * 2, "slab_bytes": slab_bytes,
                    "slab_pin_s": pin_s, "numa_node": slab.numa_node,
+                   "staging_blocks": staging_blocks,
                    "l2": f"inputs larger than L2 ({2 * B * w.bf16_block / 1e9:.1f} GB of KV "
                          "per step)",
                    "parallelism": f"dp{world} (independent per-GPU pools and slabs, no "
@@ -1011,13 +1187,17 @@ def run_ours(args) -> None:
                 "d2h_bytes_per_step": B * w.fp8_block, "ms_per_step": e2e_ms,
                 "tokens_per_s": world * 2 * B * w.block_size / (e2e_ms / 1e3),
                 "save_mode": save_mode, "restore_mode": restore_mode,
+                "issue_order": "restore first" if restore_first else "save first",
                 "pcie_GBps_per_direction": pcie_per_dir,
                 "pcie_frac_of_memcpy_d2h": pcie_per_dir / ceiling["d2h"],
                 "pcie_frac_of_memcpy_h2d": pcie_per_dir / ceiling["h2d"],
-                "pcie_frac_of_memcpy_duplex": 2 * pcie_per_dir / ceiling["duplex_total"]},
+                "pcie_frac_of_memcpy_duplex": 2 * pcie_per_dir / ceiling["duplex_total"],
+                "pcie_frac_of_memcpy_duplex_best": 2 * pcie_per_dir / ceiling["duplex_best"],
+                "memcpy_duplex_best_frac_of_solo": {
+                    "d2h": ceiling["duplex_best"] / 2 / ceiling["d2h"],
+                    "h2d": ceiling["duplex_best"] / 2 / ceiling["h2d"]}},
         "roofline": roofline,
         "bf16_kernels": bf16_kernels,
-        "cpu_baseline": cpu,
         "clocks": clocks_e2e.summary() or clocks_dev.summary(),
         # kvoff kernels launched inside the two timed regions (device step: one
         # save and one restore launch per 128 blocks; e2e: one kernel per
@@ -1026,25 +1206,55 @@ def run_ours(args) -> None:
         "gpu_launches_by_region": {"value": 2 * launches_per_call * args.steps,
                                    "e2e": launches * args.steps},
         "pcie_memcpy_ceiling_GBps": ceiling,
+        "e2e_arrangement_GBps": arrangement or None,
         "sweep_GBps": sweep,
         "dropin_e2e_GBps": dropin,
         "store_kvcache": store,
         "kv_handoff": handoff,
         "reference_gpu_path": ref_gpu,
     }
-    if rank == 0:
-        emit(line)
-    if world > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+
+
+CONFIG4_KEYS = ("value", "ms_per_step", "tokens_per_s", "e2e", "roofline", "clocks",
+                "pcie_memcpy_ceiling_GBps", "gpu_launches", "config")
 
 
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
-    else:
-        run_ours(args)
+        return
+    rank, _, world = dist_env()
+    w = make_workload(args, world)
+    # The host-core baseline runs first, before the pool, the pinned slab and
+    # the GPU work exist, so it sees the host as the reference arm does.
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_sample(w, args.cpu_seconds)
+        cpu["torch_ops_cpu"] = torch_ops_sample(w, min(5.0, args.cpu_seconds))
+    import gc
+
+    import torch
+
+    rank, local_rank, world, device = init_ranks(args)
+    line = run_ours(args, w, rank, local_rank, world, device, extras=world == 1)
+    line["cpu_baseline"] = cpu
+    if world > 1 and args.workload == "config2" and not args.no_config4:
+        # BASELINE config 4 on the same ranks: each rank's KV-head shard of a
+        # Qwen3-32B pool, 512-block restore || 512-block save (weak in blocks
+        # per rank; the pool shard shrinks as 8 / N heads).
+        gc.collect()
+        torch.cuda.empty_cache()
+        args4 = argparse.Namespace(**{**vars(args), "workload": "config4", "tp": 0, "batch": 0,
+                                      "pool_blocks": 0, "slab_gib": 0.0})
+        w4 = make_workload(args4, world)
+        line4 = run_ours(args4, w4, rank, local_rank, world, device, extras=False)
+        line["config4"] = {k: line4[k] for k in CONFIG4_KEYS}
+    if rank == 0:
+        emit(line)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
 
 
 if __name__ == "__main__":
