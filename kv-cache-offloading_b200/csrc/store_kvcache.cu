@@ -10,6 +10,18 @@
 // and stride allows) without waiting for the slot, and only the stores wait
 // for it. The grid has one CTA per kWarps rows, so the rows of a prefill of a
 // few thousand tokens are in flight in one or two waves. Offsets are 64-bit.
+//
+// The kernel is launched as a programmatic dependent of the previous kernel on
+// its stream (cudaLaunchAttributeProgrammaticStreamSerialization). Its CTAs
+// may then be scheduled while that kernel's last CTAs drain; each thread's
+// first instruction, griddepcontrol.wait, holds it until the previous kernel
+// has completed and its writes are visible, so every read of key, value and
+// slot_mapping and every cache write still follows it. Each CTA signals
+// griddepcontrol.launch_dependents once its rows are issued, so a following
+// store launched the same way overlaps this one's tail. Back to back per-layer
+// stores (36 in a Qwen3-8B forward) lose less time to launch ramp and drain.
+// After a kernel that does not signal, the launch waits for its completion as
+// usual.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -29,6 +41,7 @@ __global__ void __launch_bounds__(kThreads)
                          uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
                          int64_t row_bytes, const int32_t* __restrict__ slot_mapping,
                          int64_t num_tokens, int64_t num_slots, int32_t* bad_slots) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t vecs = row_bytes / (int64_t)sizeof(V);
   const int lane = threadIdx.x & 31;
   const int64_t rows = 2 * num_tokens;
@@ -58,17 +71,27 @@ __global__ void __launch_bounds__(kThreads)
     if (!is_v && lane == 0 && slot >= num_slots && bad_slots != nullptr)
       atomicAdd(bad_slots, 1);  // out of range: skipped, counted once per token
   }
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 template <typename V>
 int launch(const void* key, int64_t ks, const void* value, int64_t vs, void* kc, void* vc,
            int64_t row_bytes, const int32_t* slots, int64_t n, int64_t num_slots, int32_t* bad,
            cudaStream_t stream) {
-  const int64_t grid = streaming_grid(2 * n, kWarps, 0);
-  store_kvcache_kernel<V><<<grid, kThreads, 0, stream>>>(
-      static_cast<const uint8_t*>(key), ks, static_cast<const uint8_t*>(value), vs,
-      static_cast<uint8_t*>(kc), static_cast<uint8_t*>(vc), row_bytes, slots, n, num_slots, bad);
-  return cuda_status(cudaGetLastError(), "store_kvcache launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)streaming_grid(2 * n, kWarps, 0));
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(
+      cudaLaunchKernelEx(&cfg, store_kvcache_kernel<V>, static_cast<const uint8_t*>(key), ks,
+                         static_cast<const uint8_t*>(value), vs, static_cast<uint8_t*>(kc),
+                         static_cast<uint8_t*>(vc), row_bytes, slots, n, num_slots, bad),
+      "store_kvcache launch");
 }
 
 }  // namespace

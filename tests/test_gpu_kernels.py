@@ -444,3 +444,56 @@ def test_store_kvcache_graph_capture_and_bad_slots(cuda):
     untouched[idx] = False
     assert not k_cache.view(-1, h * d)[untouched].any()
     assert int(bad.item()) == 1
+
+
+def _reference_store_kvcache():
+    """The reference's own store_kvcache (nanovllm/layers/attention.py:10-40, its
+    Triton kernel and launcher) from the installed copy under baseline/_ref,
+    loaded by path without the package's model imports; None when absent."""
+    import importlib.util
+    import sys
+    import types
+
+    tree = Path(__file__).resolve().parents[1] / "baseline" / "_ref" / "nanovllm_upstream" / "nanovllm"
+    if not (tree / "layers" / "attention.py").exists():
+        return None
+    for package, path in (("nanovllm", tree), ("nanovllm.utils", tree / "utils"),
+                          ("nanovllm.layers", tree / "layers")):
+        if package not in sys.modules:
+            module = types.ModuleType(package)
+            module.__path__ = [str(path)]
+            sys.modules[package] = module
+    for name, rel in (("nanovllm.utils.context", "utils/context.py"),
+                      ("nanovllm.layers.attention", "layers/attention.py")):
+        if name not in sys.modules:
+            spec = importlib.util.spec_from_file_location(name, tree / rel)
+            module = importlib.util.module_from_spec(spec)
+            sys.modules[name] = module
+            spec.loader.exec_module(module)
+    return sys.modules["nanovllm.layers.attention"].store_kvcache
+
+
+@pytest.mark.parametrize("name", sorted(workloads.STORE_CASES))
+def test_store_kvcache_matches_the_reference_triton_kernel_on_the_gpu(cuda, name):
+    """kvoff's store and the reference's own Triton store_kvcache_kernel, both
+    run on this GPU over the same arbitrary bit patterns, leave byte-identical
+    caches (the Triton kernel moves bf16 loads and stores unchanged)."""
+    from kvoff import ops
+
+    ref_store = _reference_store_kvcache()
+    if ref_store is None:
+        pytest.skip("the reference's installed copy (baseline/_ref) is absent")
+    n, h, d, nb, bs, pad = workloads.STORE_CASES[name]
+    qkv, slots, k_in, v_in = workloads.store_kvcache_inputs(name)
+    rows = to_bf16(qkv, cuda)
+    key = rows[:, pad:pad + h * d].view(n, h, d)
+    value = rows[:, pad + h * d:].view(n, h, d)
+    slot_mapping = torch.from_numpy(slots).to(cuda)
+    caches = {}
+    for arm in ("kvoff", "reference"):
+        k_cache, v_cache = to_bf16(k_in, cuda), to_bf16(v_in, cuda)
+        store = ops.store_kvcache if arm == "kvoff" else ref_store
+        store(key, value, k_cache, v_cache, slot_mapping)
+        caches[arm] = (u16(k_cache), u16(v_cache))
+    assert np.array_equal(caches["kvoff"][0], caches["reference"][0])
+    assert np.array_equal(caches["kvoff"][1], caches["reference"][1])
