@@ -79,18 +79,72 @@ def export_kv(runner, seq: Sequence) -> KVSnapshot:
                       seq.temperature, seq.max_tokens, seq.ignore_eos, payload)
 
 
+# Host memory a verification holds at once: two pinned readback buffers of at
+# most this many bytes each (whole blocks; at least one block).
+_VERIFY_CHUNK_BYTES = 256 << 20
+
+
 @torch.inference_mode()
 def verify_imported_kv(runner, seq: Sequence, snapshot: KVSnapshot) -> bool:
-    """Byte comparison of the imported KV, one block of host readback at a time."""
-    for logical, physical in enumerate(seq.block_table):
-        start = logical * runner.block_size
-        end = min(start + runner.block_size, snapshot.num_cached_tokens)
-        actual = runner.kv_cache[:, :, physical, :end - start].cpu()
-        expected = snapshot.kv[:, :, start:end]
-        if not torch.equal(actual.view(torch.uint8), expected.view(torch.uint8)):
-            return False
-        del actual
-    return True
+    """True when the sequence's blocks hold exactly the snapshot's KV bytes.
+
+    CUDA pool: the written tokens come back in chunks of whole blocks, each
+    chunk one strided DMA per block into a pinned dense buffer
+    (kvoff_copy_tokens, as in export_kv); two buffers alternate, so the next
+    chunk's DMA runs while the host compares the previous one. Host memory
+    stays bounded (two buffers of about _VERIFY_CHUNK_BYTES) however long the
+    sequence is. A CPU pool is gathered and compared in one pass. Missing
+    blocks compare unequal.
+    """
+    cache = runner.kv_cache
+    count = snapshot.num_cached_tokens
+    block_size = runner.block_size
+    num_blocks = -(-count // block_size)
+    block_ids = list(seq.block_table[:num_blocks])
+    expected = snapshot.kv.view(torch.uint8)
+    if len(block_ids) < num_blocks or snapshot.kv.dtype != cache.dtype:
+        return False
+    if count <= 0:
+        return True
+    if not cache.is_cuda:
+        index = torch.tensor(block_ids, dtype=torch.int64)
+        actual = cache.index_select(2, index).flatten(2, 3)[:, :, :count]
+        return torch.equal(actual.view(torch.uint8), expected)
+    from kvoff import ops
+
+    token_bytes = 2 * cache.shape[1] * cache.shape[-2] * cache.shape[-1] * cache.element_size()
+    chunk_blocks = max(1, _VERIFY_CHUNK_BYTES // (block_size * token_bytes))
+    chunk_tokens = chunk_blocks * block_size
+    chunks = -(-count // chunk_tokens)
+    shape = (2, cache.shape[1], min(count, chunk_tokens), *cache.shape[-2:])
+    buffers = [torch.empty(shape, dtype=cache.dtype, pin_memory=True)
+               for _ in range(min(2, chunks))]
+    stream = torch.cuda.current_stream(cache.device)
+    landed = [torch.cuda.Event() for _ in buffers]
+
+    def issue(k: int):
+        first = k * chunk_tokens
+        n = min(chunk_tokens, count - first)
+        ops.copy_tokens(cache, block_ids[k * chunk_blocks:], n, buffers[k % 2].data_ptr(),
+                        stream=stream)
+        landed[k % 2].record(stream)
+
+    issue(0)
+    try:
+        for k in range(chunks):
+            if k + 1 < chunks:  # its buffer's previous chunk was compared last iteration
+                issue(k + 1)
+            landed[k % 2].synchronize()
+            first = k * chunk_tokens
+            n = min(chunk_tokens, count - first)
+            # The DMA wrote a dense [2, L, n, H, D] run at the buffer's start.
+            actual = buffers[k % 2].view(-1)[:2 * cache.shape[1] * n * shape[3] * shape[4]]
+            actual = actual.view(2, cache.shape[1], n, *shape[3:])
+            if not torch.equal(actual.view(torch.uint8), expected[:, :, first:first + n]):
+                return False
+        return True
+    finally:
+        stream.synchronize()  # no DMA may still target a buffer when it is freed
 
 
 @torch.inference_mode()

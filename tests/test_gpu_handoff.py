@@ -165,3 +165,38 @@ def test_import_validation_matches_the_reference(cuda, handoff):
     runner.world_size = 2
     with pytest.raises(NotImplementedError, match="tensor_parallel_size=1"):
         handoff.import_kv(runner, manager, bad)
+
+
+@pytest.mark.parametrize("chunk_blocks", [1, 2, 64])
+def test_verify_imported_kv_reads_back_in_chunks_and_finds_any_changed_byte(
+        cuda, handoff, monkeypatch, chunk_blocks):
+    """verify_imported_kv compares every written token: in one chunk, or in
+    chunks of whole blocks through two alternating pinned buffers."""
+    shape, count = (2, 2, 6, 16, 2, 8), 70  # 5 blocks, the last one partial
+    token_bytes = 2 * shape[1] * shape[4] * shape[5] * 2
+    monkeypatch.setattr(handoff, "_VERIFY_CHUNK_BYTES", chunk_blocks * shape[3] * token_bytes)
+    g = torch.Generator().manual_seed(3)
+    pool = torch.randn(shape, generator=g).to(torch.bfloat16).to(cuda)
+    runner = SimpleNamespace(world_size=1, block_size=shape[3], kv_cache=pool)
+    seq = Sequence(list(range(count - 1)), SamplingParams(max_tokens=64))
+    seq.append_token(5)
+    seq.append_token(6)
+    seq.status = SequenceStatus.RUNNING
+    seq.num_cached_tokens = count
+    seq.block_table = [5, 0, 3, 1, 4]
+    snapshot = handoff.export_kv(runner, seq)
+    assert handoff.verify_imported_kv(runner, seq, snapshot)
+    # One changed byte anywhere among the written tokens is found: first block,
+    # a middle block, the last written token of the partial block.
+    for block, token in ((5, 0), (3, 7), (4, count - 4 * shape[3] - 1)):
+        saved = pool[1, 1, block, token].clone()
+        pool[1, 1, block, token, 1, 2] += 1
+        assert not handoff.verify_imported_kv(runner, seq, snapshot)
+        pool[1, 1, block, token] = saved
+    assert handoff.verify_imported_kv(runner, seq, snapshot)
+    # Tokens past the written count are not part of the snapshot.
+    pool[0, 0, 4, count - 4 * shape[3]:] = 9
+    assert handoff.verify_imported_kv(runner, seq, snapshot)
+    # A block table without room for every written token does not verify.
+    seq.block_table = seq.block_table[:-1]
+    assert not handoff.verify_imported_kv(runner, seq, snapshot)
