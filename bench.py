@@ -135,8 +135,9 @@ def parse_args():
     p.add_argument("--no-dropin", action="store_true",
                    help="skip the per-block vs batched CPUBlockCache measurement")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
-    p.add_argument("--staging-blocks", type=int, default=16,
-                   help="FP8 staging depth of the e2e step before the arrangement sweep")
+    p.add_argument("--staging-blocks", type=int, default=64,
+                   help="FP8 staging depth (blocks) of the e2e step; at N=1 the arrangement "
+                        "sweep may pick another")
     p.add_argument("--no-config4", action="store_true",
                    help="at N > 1, skip the extra config-4 (KV-head sharded) measurement")
     args = p.parse_args()
@@ -620,7 +621,44 @@ def handoff_bench(torch, w: Workload, pool, args) -> dict:
         out[name] = {"ms": 1e3 * sec, "GBps": nbytes / sec / 1e9}
     out["export_bytes_equal"] = bool(torch.equal(pinned.view(torch.int16),
                                                  snapshot["kv"].view(torch.int16)))
+    # verify_imported_kv after the import (dst now holds the snapshot): kvoff's
+    # drop-in against the reference's own function, on the same blocks.
+    ours_import()
+    out["verify"] = handoff_verify(torch, w, pool, dst, count, pinned, seconds)
     del pinned, snapshot
+    return out
+
+
+def handoff_verify(torch, w: Workload, pool, block_ids, count, snapshot_kv, seconds) -> dict:
+    """Time verify_imported_kv (nanovllm/engine/kv_handoff.py:63-78) on an
+    imported sequence: kvoff's drop-in (chunked native readback) and the
+    reference's (one synchronous block readback at a time), both loaded with
+    the reference's own engine modules from its installed copy."""
+    import importlib
+    from types import SimpleNamespace
+
+    try:
+        for dep in ("nanovllm.sampling_params", "nanovllm.engine.sequence",
+                    "nanovllm.engine.handoff_timing"):
+            if reference_module(dep) is None:
+                return {"unavailable": "the reference's installed copy (baseline/_ref) is absent"}
+        ours = importlib.import_module("kvoff.kv_handoff")
+        reference = reference_module("nanovllm.engine.kv_handoff")
+    except Exception as exc:  # context only; never fails the bench
+        return {"error": f"{type(exc).__name__}: {str(exc)[:200]}"}
+    runner = SimpleNamespace(world_size=1, block_size=w.block_size, kv_cache=pool)
+    seq = SimpleNamespace(block_table=list(block_ids))
+    snap = SimpleNamespace(num_cached_tokens=count, kv=snapshot_kv)
+    nbytes = snapshot_kv.numel() * snapshot_kv.element_size()
+    out = {}
+    for name, module in (("kvoff", ours), ("reference", reference)):
+        result = {}
+
+        def run(module=module, result=result):
+            result["equal"] = bool(module.verify_imported_kv(runner, seq, snap))
+
+        sec = seconds(run, reps=3)
+        out[name] = {"ms": 1e3 * sec, "GBps": nbytes / sec / 1e9, "verified": result["equal"]}
     return out
 
 
