@@ -54,12 +54,12 @@ for _p in (ROOT, ROOT / "kv-cache-offloading_b200"):
 SWEEP_BATCHES = (1, 8, 32, 128)
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "KV restore+save GB/s (FP8, bf16-equivalent bytes)"
-# dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of the save
-# kernel on 8 config-2 blocks (profiles/fp8_save_kernel_config2.md), per byte of
-# bf16 block read; traffic scales with blocks because each is read and written once.
-SAVE_KERNEL_DRAM_BYTES_PER_BF16_BYTE = (302_021_632 + 100_535_552) / (8 * 37_748_736)
-TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one 8-block launch "
-                  "(profiles/fp8_save_kernel_config2.md), scaled by blocks per launch")
+# dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of a full
+# 128-block config-2 launch of the save kernel (profiles/fp8_save_kernel_config2.md),
+# per byte of bf16 block read; other batch sizes scale it by blocks per launch.
+SAVE_KERNEL_DRAM_BYTES_PER_BF16_BYTE = (4_832_047_616 + 2_400_740_352) / (128 * 37_748_736)
+TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one 128-block config-2 "
+                  "launch (profiles/fp8_save_kernel_config2.md), scaled by blocks per launch")
 
 
 @dataclass(frozen=True)
