@@ -434,6 +434,13 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
     2 KB row write opens its own DRAM page). Every 97th token is padding (-1).
     Algorithmic bytes per token and layer: K and V rows read and written
     (4 * H * D * 2) plus the 4-byte slot.
+
+    Three timings per arm (kvoff and the reference's own Triton kernel):
+    eager (one Python call per layer); graph (the 36 stores back to back in a
+    CUDA graph, sources in HBM); forward (each layer's store between a kernel
+    that writes that layer's qkv rows and a kernel that reads them, 36 layers
+    in a CUDA graph, as the engine runs it; reported as the time the store
+    adds over the same chain without it, with the rows fresh in L2).
     """
     from kvoff import ops
 
@@ -459,6 +466,7 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
     per_step = w.layers * tokens * (4 * kv_width * 2 + 4)
     out = {"tokens": tokens, "layers": w.layers, "algorithmic_bytes_per_step": per_step}
     ref_store = reference_store_kvcache()
+    sink = torch.empty((w.layers, tokens, kv_width), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.current_stream(device)
     bad = torch.zeros(1, dtype=torch.int32, device=device)
     for pattern, slots in patterns.items():
@@ -497,10 +505,29 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
             stream.wait_stream(side)
             return graph
 
-        arms = [("kvoff", ours)] + ([("reference_triton", reference)] if callable(ref_store)
-                                    else [])
+        def forward(store_layer):
+            def run():
+                for layer in range(w.layers):
+                    qkv[layer].mul_(1.0)  # the kernel that writes the layer's rows
+                    store_layer(layer)
+                    sink[layer].copy_(qkv[layer, :, :kv_width])  # a kernel after it
+            return run
+
+        def ours_layer(layer, slots=slots):
+            ops.store_kvcache(keys[layer], values[layer], caches[0, layer], caches[1, layer],
+                              slots)
+
+        def reference_layer(layer, slots=slots):
+            ref_store(keys[layer], values[layer], caches[0, layer], caches[1, layer], slots)
+
+        arms = [("kvoff", ours, ours_layer)]
+        if callable(ref_store):
+            arms.append(("reference_triton", reference, reference_layer))
         res = {}
-        for arm, fn in arms:
+        graph = captured(forward(lambda layer: None))
+        bare_ms = Timer(torch, stream, 1).run(graph.replay, args.steps, args.warmup) / args.steps
+        del graph
+        for arm, fn, layer_fn in arms:
             graph = captured(fn)
             for mode, run in (("eager", fn), ("graph", graph.replay)):
                 ms = Timer(torch, stream, 1).run(run, args.steps, args.warmup) / args.steps
@@ -508,6 +535,13 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
                                         "us_per_launch": 1e3 * ms / w.layers,
                                         "frac_of_hbm_peak": per_step / (ms / 1e3) / 1e9
                                         / hbm_peak}
+            del graph
+            graph = captured(forward(layer_fn))
+            ms = Timer(torch, stream, 1).run(graph.replay, args.steps, args.warmup) / args.steps
+            added = ms - bare_ms
+            res[f"{arm}_forward"] = {"ms_per_step": ms, "ms_without_store": bare_ms,
+                                     "us_added_per_layer": 1e3 * added / w.layers,
+                                     "GBps": per_step / (added / 1e3) / 1e9}
             del graph
         ms = Timer(torch, stream, 1).run(torch_scatter, args.steps, args.warmup) / args.steps
         res["torch_index_put"] = {"ms_per_step": ms, "GBps": per_step / (ms / 1e3) / 1e9,
@@ -518,7 +552,7 @@ def store_kvcache_bench(torch, w: Workload, pool, args, hbm_peak: float) -> dict
         out[pattern] = res
     torch.cuda.synchronize()
     out["bad_slots"] = int(bad.item())
-    del keys, values, qkv
+    del keys, values, qkv, sink
     return out
 
 

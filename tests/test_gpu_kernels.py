@@ -497,3 +497,37 @@ def test_store_kvcache_matches_the_reference_triton_kernel_on_the_gpu(cuda, name
         caches[arm] = (u16(k_cache), u16(v_cache))
     assert np.array_equal(caches["kvoff"][0], caches["reference"][0])
     assert np.array_equal(caches["kvoff"][1], caches["reference"][1])
+
+
+@pytest.mark.parametrize("heads,dim,offset", [(2, 128, 0), (4, 128, 0), (8, 256, 0), (8, 128, 4),
+                                              (3, 80, 0)])
+def test_store_kvcache_row_shapes(cuda, heads, dim, offset):
+    """Rows of 512 B, 1 KB (the row kernel at 32 / 64 threads per token), 4 KB
+    (the general kernel, two vectors per thread), a source 8-byte aligned only
+    (the general kernel at 8-byte vectors) and a 480-byte row: every valid token
+    lands byte for byte, skipped and out-of-range slots leave the cache as it was."""
+    from kvoff import ops
+
+    n, nb, bs = 200, 6, 64
+    row = heads * dim
+    torch.manual_seed(heads * 1000 + dim + offset)
+    raw = torch.randn(n * (2 * row + 8) + 8, device=cuda).to(torch.bfloat16)
+    qkv = raw[offset:offset + n * (2 * row + 8)].view(n, 2 * row + 8)
+    key = qkv[:, 8:8 + row].view(n, heads, dim)
+    value = qkv[:, 8 + row:].view(n, heads, dim)
+    k_cache = torch.randn(nb, bs, heads, dim, device=cuda).to(torch.bfloat16)
+    v_cache = torch.randn_like(k_cache)
+    k_want, v_want = k_cache.clone(), v_cache.clone()
+    slots = torch.randperm(nb * bs, device=cuda)[:n].to(torch.int32)
+    slots[::7] = -1
+    slots[5] = nb * bs + 1
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda)
+    ops.store_kvcache(key, value, k_cache, v_cache, slots, bad_slots=bad)
+    valid = (slots >= 0) & (slots < nb * bs)
+    idx = slots[valid].long()
+    k_want.view(-1, row)[idx] = key.reshape(n, -1)[valid]
+    v_want.view(-1, row)[idx] = value.reshape(n, -1)[valid]
+    torch.cuda.synchronize()
+    assert torch.equal(k_cache.view(torch.int16), k_want.view(torch.int16))
+    assert torch.equal(v_cache.view(torch.int16), v_want.view(torch.int16))
+    assert int(bad.item()) == 1
