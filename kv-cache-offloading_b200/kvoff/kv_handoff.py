@@ -79,72 +79,66 @@ def export_kv(runner, seq: Sequence) -> KVSnapshot:
                       seq.temperature, seq.max_tokens, seq.ignore_eos, payload)
 
 
-# Host memory a verification holds at once: two pinned readback buffers of at
-# most this many bytes each (whole blocks; at least one block).
-_VERIFY_CHUNK_BYTES = 256 << 20
+# Device memory a verification of a CUDA pool holds at once: two buffers (the
+# pool's tokens and the snapshot's) of at most this many bytes each (whole
+# blocks; at least one block).
+_VERIFY_CHUNK_BYTES = 128 << 20
 
 
 @torch.inference_mode()
 def verify_imported_kv(runner, seq: Sequence, snapshot: KVSnapshot) -> bool:
     """True when the sequence's blocks hold exactly the snapshot's KV bytes.
 
-    CUDA pool: the written tokens come back in chunks of whole blocks, each
-    chunk one strided DMA per block into a pinned dense buffer
-    (kvoff_copy_tokens, as in export_kv); two buffers alternate, so the next
-    chunk's DMA runs while the host compares the previous one. Host memory
-    stays bounded (two buffers of about _VERIFY_CHUNK_BYTES) however long the
-    sequence is. A CPU pool is gathered and compared in one pass. Missing
-    blocks compare unequal.
+    CUDA pool: the comparison runs on the GPU, in chunks of whole blocks. For
+    each chunk the sequence's tokens are gathered device to device into one
+    dense buffer (kvoff_copy_tokens, as export_kv does into host memory), the
+    snapshot's matching tokens are copied host to device into another (one
+    contiguous copy per (K/V, layer) row of the snapshot), and a device-side
+    byte comparison folds into one flag that the host reads once at the end.
+    So the snapshot crosses PCIe once and the host does no byte work; device
+    memory stays bounded (two buffers of about _VERIFY_CHUNK_BYTES) however
+    long the sequence is. A CPU pool is gathered and compared in one pass.
+    Missing blocks, or a snapshot of another shape or dtype, compare unequal.
     """
     cache = runner.kv_cache
     count = snapshot.num_cached_tokens
     block_size = runner.block_size
     num_blocks = -(-count // block_size)
     block_ids = list(seq.block_table[:num_blocks])
-    expected = snapshot.kv.view(torch.uint8)
-    if len(block_ids) < num_blocks or snapshot.kv.dtype != cache.dtype:
+    kv = snapshot.kv
+    if len(block_ids) < num_blocks or kv.dtype != cache.dtype:
         return False
     if count <= 0:
         return True
+    if tuple(kv.shape) != (2, cache.shape[1], count, *cache.shape[-2:]):
+        return False
     if not cache.is_cuda:
         index = torch.tensor(block_ids, dtype=torch.int64)
         actual = cache.index_select(2, index).flatten(2, 3)[:, :, :count]
-        return torch.equal(actual.view(torch.uint8), expected)
+        return torch.equal(actual.view(torch.uint8), kv.view(torch.uint8))
     from kvoff import ops
 
-    token_bytes = 2 * cache.shape[1] * cache.shape[-2] * cache.shape[-1] * cache.element_size()
-    chunk_blocks = max(1, _VERIFY_CHUNK_BYTES // (block_size * token_bytes))
+    kv = kv if kv.is_contiguous() else kv.contiguous()
+    layers, (heads, dim) = cache.shape[1], cache.shape[-2:]
+    row_bytes = heads * dim * cache.element_size()  # one token of one (K/V, layer) row
+    chunk_blocks = max(1, _VERIFY_CHUNK_BYTES // (2 * layers * block_size * row_bytes))
     chunk_tokens = chunk_blocks * block_size
-    chunks = -(-count // chunk_tokens)
-    shape = (2, cache.shape[1], min(count, chunk_tokens), *cache.shape[-2:])
-    buffers = [torch.empty(shape, dtype=cache.dtype, pin_memory=True)
-               for _ in range(min(2, chunks))]
-    stream = torch.cuda.current_stream(cache.device)
-    landed = [torch.cuda.Event() for _ in buffers]
-
-    def issue(k: int):
-        first = k * chunk_tokens
+    width = min(count, chunk_tokens)
+    actual = torch.empty((2 * layers * width * heads * dim,), dtype=cache.dtype,
+                         device=cache.device)
+    expected = torch.empty_like(actual)
+    differs = torch.zeros((), dtype=torch.bool, device=cache.device)
+    rows = kv.view(2 * layers, count, heads, dim)
+    for first in range(0, count, chunk_tokens):
         n = min(chunk_tokens, count - first)
-        ops.copy_tokens(cache, block_ids[k * chunk_blocks:], n, buffers[k % 2].data_ptr(),
-                        stream=stream)
-        landed[k % 2].record(stream)
-
-    issue(0)
-    try:
-        for k in range(chunks):
-            if k + 1 < chunks:  # its buffer's previous chunk was compared last iteration
-                issue(k + 1)
-            landed[k % 2].synchronize()
-            first = k * chunk_tokens
-            n = min(chunk_tokens, count - first)
-            # The DMA wrote a dense [2, L, n, H, D] run at the buffer's start.
-            actual = buffers[k % 2].view(-1)[:2 * cache.shape[1] * n * shape[3] * shape[4]]
-            actual = actual.view(2, cache.shape[1], n, *shape[3:])
-            if not torch.equal(actual.view(torch.uint8), expected[:, :, first:first + n]):
-                return False
-        return True
-    finally:
-        stream.synchronize()  # no DMA may still target a buffer when it is freed
+        here = actual[:2 * layers * n * heads * dim]
+        want = expected[:2 * layers * n * heads * dim].view(2 * layers, n, heads, dim)
+        ops.copy_tokens(cache, block_ids[first // block_size:], n, here.data_ptr())
+        for r in range(2 * layers):
+            ops.memcpy(want[r].data_ptr(), rows[r, first].data_ptr(), n * row_bytes,
+                       device=cache.device)
+        differs |= torch.ne(here.view(torch.uint8), want.view(-1).view(torch.uint8)).any()
+    return not bool(differs.item())
 
 
 @torch.inference_mode()

@@ -170,8 +170,8 @@ def test_import_validation_matches_the_reference(cuda, handoff):
 @pytest.mark.parametrize("chunk_blocks", [1, 2, 64])
 def test_verify_imported_kv_reads_back_in_chunks_and_finds_any_changed_byte(
         cuda, handoff, monkeypatch, chunk_blocks):
-    """verify_imported_kv compares every written token: in one chunk, or in
-    chunks of whole blocks through two alternating pinned buffers."""
+    """verify_imported_kv compares every written token, in one chunk or in
+    chunks of whole blocks, on the device; one changed byte anywhere fails it."""
     shape, count = (2, 2, 6, 16, 2, 8), 70  # 5 blocks, the last one partial
     token_bytes = 2 * shape[1] * shape[4] * shape[5] * 2
     monkeypatch.setattr(handoff, "_VERIFY_CHUNK_BYTES", chunk_blocks * shape[3] * token_bytes)
@@ -200,3 +200,12 @@ def test_verify_imported_kv_reads_back_in_chunks_and_finds_any_changed_byte(
     # A block table without room for every written token does not verify.
     seq.block_table = seq.block_table[:-1]
     assert not handoff.verify_imported_kv(runner, seq, snapshot)
+    # A snapshot of another length does not verify (and is not read past its end).
+    shorter = handoff.KVSnapshot(snapshot.token_ids, snapshot.num_prompt_tokens, count,
+                                 snapshot.block_size, 1.0, 64, False, snapshot.kv[:, :, :-1])
+    seq.block_table = [5, 0, 3, 1, 4]
+    assert not handoff.verify_imported_kv(runner, seq, shorter)
+    # A pageable snapshot verifies the same way.
+    pageable = handoff.KVSnapshot(snapshot.token_ids, snapshot.num_prompt_tokens, count,
+                                  snapshot.block_size, 1.0, 64, False, snapshot.kv.clone())
+    assert handoff.verify_imported_kv(runner, seq, pageable)
