@@ -659,6 +659,7 @@ def handoff_bench(torch, w: Workload, pool, args) -> dict:
     # drop-in against the reference's own function, on the same blocks.
     ours_import()
     out["verify"] = handoff_verify(torch, w, pool, dst, count, pinned, seconds)
+    out["verify_ms"] = out["verify"].get("kvoff", {}).get("ms")
     del pinned, snapshot
     return out
 
