@@ -130,9 +130,10 @@ int launch(const void* key, int64_t ks, const void* value, int64_t vs, void* kc,
   const int64_t vecs = row_bytes / (int64_t)sizeof(V);
   if (sizeof(V) == 16 && (vecs == 32 || vecs == 64 || vecs == 128)) {
     // Every offset the row kernel forms must fit in 32 bits.
+    constexpr int64_t kMax = 0xFFFFFFFFll;
     const int64_t stride = ks > vs ? ks : vs;
-    const bool fits = n * stride + row_bytes <= 0xFFFFFFFFll &&
-                      num_slots * row_bytes <= 0xFFFFFFFFll && num_slots <= 0x7FFFFFFFll;
+    const bool fits = stride <= (kMax - row_bytes) / n && num_slots <= kMax / row_bytes &&
+                      num_slots <= 0x7FFFFFFFll;
     if (fits) {
       if (vecs == 128)
         return launch_rows<128>(key, ks, value, vs, kc, vc, slots, n, num_slots, bad, stream);
